@@ -1,0 +1,102 @@
+"""ctypes binding of libfkb200.so, the C ABI declared in include/fkb200.h.
+
+The library is loaded on first use.  If it has not been built, every op raises
+RuntimeError: there is no CPU fallback for any op in this package.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import threading
+from pathlib import Path
+
+import torch
+
+LIB_PATH = Path(__file__).resolve().parent / "_lib" / "libfkb200.so"
+
+FK_F32, FK_F16, FK_BF16 = 0, 1, 2
+_DTYPE_CODES = {torch.float32: FK_F32, torch.float16: FK_F16, torch.bfloat16: FK_BF16}
+
+_vp, _i64, _i32, _f32, _sz = C.c_void_p, C.c_int64, C.c_int, C.c_float, C.c_size_t
+
+# name -> argtypes (restype is int status unless listed in _RESTYPES)
+SIGNATURES: dict[str, list] = {
+    "fk_version": [],
+    "fk_status_string": [_i32],
+    "fk_last_error": [],
+    "fk_swiglu_fwd": [_vp, _vp, _vp, _i64, _i32, _vp],
+    "fk_swiglu_bwd": [_vp, _vp, _vp, _vp, _vp, _i64, _i32, _vp],
+    "fk_rmsnorm_fwd": [_vp, _i64, _vp, _i32, _vp, _i64, _vp, _i64, _i64, _f32, _i32, _vp],
+    "fk_rmsnorm_bwd_workspace_size": [_i64, _i64, C.POINTER(_sz)],
+    "fk_rmsnorm_bwd": [_vp, _vp, _vp, _i32, _vp, _vp, _vp, _vp, _sz, _i64, _i64, _i32, _vp],
+    "fk_router_fwd": [_vp, _i64, _i32, _i64, _i32, _i32, _vp, _vp, _vp],
+    "fk_router_bwd": [_vp, _vp, _vp, _vp, _i64, _i32, _i32, _vp],
+    "fk_ce_fwd": [_vp, _i64, _vp, _i64, _vp, _i64, _i64, _i64, _f32, _i32, _vp, _vp, _vp, _vp,
+                  _vp],
+    "fk_ce_bwd_scale": [_vp, _i64, _i64, _i64, _vp, _i32, _vp],
+}
+_RESTYPES = {"fk_status_string": C.c_char_p, "fk_last_error": C.c_char_p}
+
+_lib = None
+_lock = threading.Lock()
+
+
+def load() -> C.CDLL:
+    """Load libfkb200.so (once) and attach the declared signatures."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is None:
+            if not LIB_PATH.exists():
+                raise RuntimeError(
+                    f"{LIB_PATH} is not built; run `python -m fusedkernels_b200._build` "
+                    "(fusedkernels_b200 has no CPU fallback)")
+            lib = C.CDLL(str(LIB_PATH))
+            for name, args in SIGNATURES.items():
+                fn = getattr(lib, name)
+                fn.argtypes = args
+                fn.restype = _RESTYPES.get(name, C.c_int)
+            _lib = lib
+    return _lib
+
+
+def check(status: int, name: str) -> None:
+    if status != 0:
+        lib = load()
+        msg = lib.fk_last_error().decode(errors="replace")
+        raise RuntimeError(f"{name} failed ({lib.fk_status_string(status).decode()}): {msg}")
+
+
+def call(name: str, *args) -> None:
+    """Call a status-returning entry point and raise RuntimeError on failure."""
+    check(getattr(load(), name)(*args), name)
+
+
+def dtype_code(dtype: torch.dtype) -> int:
+    try:
+        return _DTYPE_CODES[dtype]
+    except KeyError:
+        raise TypeError(f"unsupported dtype {dtype}; expected float32, float16 or bfloat16")
+
+
+def stream_of(t: torch.Tensor) -> int:
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+_ws_cache: dict = {}
+
+
+def rmsnorm_bwd_workspace_bytes(rows: int, cols: int, device: torch.device) -> int:
+    key = (rows, cols, device.index)
+    v = _ws_cache.get(key)
+    if v is None:
+        out = C.c_size_t(0)
+        with torch.cuda.device(device):
+            check(load().fk_rmsnorm_bwd_workspace_size(rows, cols, C.byref(out)),
+                  "fk_rmsnorm_bwd_workspace_size")
+        v = _ws_cache[key] = out.value
+    return v

@@ -1,0 +1,460 @@
+// Fused cross-entropy forward + gradient, reference cross_entropy.py:24-116.
+//
+// HBM traffic is one read of the logits and one write of the gradient.  A row of V
+// logits (250.5 KiB for V=128256 bf16) is larger than one SM's shared memory, so a
+// thread-block CLUSTER of C CTAs (C <= 8) owns a row: CTA c bulk-copies (cp.async.bulk,
+// mbarrier-completed) its 1/C slice of the row into shared memory, reduces it to
+// (max, sum exp, sum x, target logit), and the C partials are exchanged through
+// distributed shared memory.  Every CTA combines the partials in rank order (so all CTAs
+// hold bit-identical statistics), then writes the gradient of its slice straight from
+// shared memory.  Nothing is re-read from HBM.  Clusters are persistent and walk rows
+// r = cluster_id, += n_clusters; partial slots are double-buffered by row parity so one
+// cluster barrier per row suffices.
+//
+// The mean-reduction scale 1/n_valid is folded into the gradient write (n_valid comes
+// from a one-CTA prologue that counts non-ignored targets), and the scalar loss is a
+// fixed-order reduction of the per-row losses (deterministic).  Rows longer than
+// 8 x 200 KiB fall back to a three-sweep kernel that re-reads the row from global memory.
+#include "common.cuh"
+#include "ptx.cuh"
+
+namespace fk {
+namespace {
+
+constexpr int kCeThreads = 256;
+constexpr int kMaxClusterBytes = 40 * 1024;   // target slice size per CTA
+constexpr int kMaxSliceBytes = 200 * 1024;    // hard cap (dynamic shared memory)
+constexpr uint32_t kBulkPiece = 32 * 1024;    // bytes per cp.async.bulk instruction
+
+template <typename T>
+__device__ __forceinline__ float fexp(float x) { return __expf(x); }
+template <>
+__device__ __forceinline__ float fexp<float>(float x) { return expf(x); }
+
+__global__ void ce_prologue(const int64_t* __restrict__ targets, int64_t n_rows,
+                            int64_t ignore_index, int* __restrict__ n_valid,
+                            int* __restrict__ err) {
+  __shared__ int red[32];
+  int c = 0;
+  for (int64_t i = threadIdx.x; i < n_rows; i += blockDim.x) c += (targets[i] != ignore_index);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) c += __shfl_xor_sync(0xffffffffu, c, o);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = c;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int tot = 0;
+    for (int i = 0; i < (int)(blockDim.x >> 5); ++i) tot += red[i];
+    *n_valid = tot < 1 ? 1 : tot;
+    *err = 0;
+  }
+}
+
+__global__ void ce_finalize(const float* __restrict__ loss_rows, int64_t n_rows,
+                            const int* __restrict__ n_valid, float* __restrict__ loss) {
+  __shared__ float red[32];
+  float s = 0.f;
+  for (int64_t i = threadIdx.x; i < n_rows; i += blockDim.x) s += loss_rows[i];
+  s = warp_sum(s);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float tot = 0.f;
+    for (int i = 0; i < (int)(blockDim.x >> 5); ++i) tot += red[i];
+    *loss = tot / (float)(*n_valid);
+  }
+}
+
+// Block-wide reductions of up to 4 floats (max for slot 0 when kMax, else sums).
+__device__ __forceinline__ float block_max(float v, float* red) {
+  v = warp_max(v);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  __syncthreads();
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  float m = red[0];
+  for (int i = 1; i < (int)(blockDim.x >> 5); ++i) m = fmaxf(m, red[i]);
+  return m;
+}
+__device__ __forceinline__ float2 block_sum2(float a, float b, float* red) {
+  a = warp_sum(a);
+  b = warp_sum(b);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  __syncthreads();
+  if (lane == 0) {
+    red[warp] = a;
+    red[32 + warp] = b;
+  }
+  __syncthreads();
+  float sa = 0.f, sb = 0.f;
+  for (int i = 0; i < (int)(blockDim.x >> 5); ++i) {
+    sa += red[i];
+    sb += red[32 + i];
+  }
+  return make_float2(sa, sb);
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kCeThreads) ce_cluster_kernel(
+    const T* __restrict__ logits, int64_t lstride, T* grad, int64_t gstride,
+    const int64_t* __restrict__ targets, int64_t n_rows, int n_cols, int64_t ignore_index,
+    float lsm, const int* __restrict__ n_valid_p, float* __restrict__ loss_rows,
+    int* __restrict__ err, int chunk, int bulk, int gvec) {
+  constexpr int VN = 16 / sizeof(T);
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  T* buf = reinterpret_cast<T*>(smem_raw);
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ float slots[2][4];  // [row parity] {max, sum exp, sum x, target logit}
+  __shared__ float red[64];
+  __shared__ float stats[4];     // combined {lse, sum x, target logit, unused}
+
+  const int tid = threadIdx.x;
+  const uint32_t crank = ptx::cluster_ctarank();
+  const uint32_t csize = ptx::cluster_nctarank();
+  const int64_t c0 = (int64_t)crank * chunk;
+  int my_len = (int)((int64_t)n_cols - c0);
+  if (my_len > chunk) my_len = chunk;
+  if (my_len < 0) my_len = 0;
+  const int bulk_len = bulk ? (my_len / VN) * VN : 0;
+  const uint32_t bulk_bytes = (uint32_t)bulk_len * sizeof(T);
+
+  if (tid == 0) {
+    ptx::mbar_init(&bar, 1);
+    ptx::fence_mbar_init();
+  }
+  __syncthreads();
+
+  const float inv_nv = 1.0f / (float)(*n_valid_p);
+  const float smooth = lsm / (float)n_cols;
+  uint32_t phase = 0;
+  int par = 0;
+  for (int64_t row = ptx::cluster_id_x(); row < n_rows; row += ptx::nclusters_x(), par ^= 1) {
+    const T* src = logits + row * lstride + c0;
+    if (tid == 0 && bulk_len > 0) {
+      ptx::fence_proxy_async_smem();
+      ptx::mbar_arrive_expect_tx(&bar, bulk_bytes);
+      for (uint32_t off = 0; off < bulk_bytes; off += kBulkPiece) {
+        uint32_t n = bulk_bytes - off < kBulkPiece ? bulk_bytes - off : kBulkPiece;
+        ptx::bulk_g2s(reinterpret_cast<unsigned char*>(buf) + off,
+                      reinterpret_cast<const unsigned char*>(src) + off, n, &bar);
+      }
+    }
+    for (int i = bulk_len + tid; i < my_len; i += kCeThreads) buf[i] = src[i];
+    const int64_t t = targets[row];
+    bool poisoned = false;
+    if (bulk_len > 0) {
+      if (!ptx::mbar_wait(&bar, phase)) {
+        poisoned = true;  // copy never completed: report, keep cluster barriers aligned
+        atomicExch(err, 2);
+      }
+      phase ^= 1;
+    }
+    __syncthreads();
+
+    // Pass 1: slice max.  Pass 2: slice sum of exp(x - max) and sum of x.
+    const int nvec = my_len / VN;
+    float m = -INFINITY;
+    for (int v = tid; v < nvec; v += kCeThreads) {
+      Vec16<T> p;
+      p.u = reinterpret_cast<const uint4*>(buf)[v];
+#pragma unroll
+      for (int e = 0; e < VN; ++e) m = fmaxf(m, Elt<T>::to_f(p.e[e]));
+    }
+    for (int i = nvec * VN + tid; i < my_len; i += kCeThreads) m = fmaxf(m, Elt<T>::to_f(buf[i]));
+    const float mc = block_max(m, red);
+    float s = 0.f, sx = 0.f;
+    if (mc != -INFINITY) {
+      for (int v = tid; v < nvec; v += kCeThreads) {
+        Vec16<T> p;
+        p.u = reinterpret_cast<const uint4*>(buf)[v];
+#pragma unroll
+        for (int e = 0; e < VN; ++e) {
+          float x = Elt<T>::to_f(p.e[e]);
+          s += fexp<T>(x - mc);
+          sx += x;
+        }
+      }
+      for (int i = nvec * VN + tid; i < my_len; i += kCeThreads) {
+        float x = Elt<T>::to_f(buf[i]);
+        s += fexp<T>(x - mc);
+        sx += x;
+      }
+    } else {
+      for (int i = tid; i < my_len; i += kCeThreads) sx += Elt<T>::to_f(buf[i]);
+    }
+    const float2 ssum = block_sum2(s, sx, red);
+    if (tid == 0) {
+      float xt = 0.f;
+      if (t >= c0 && t < c0 + my_len) xt = Elt<T>::to_f(buf[t - c0]);
+      slots[par][0] = mc;
+      slots[par][1] = ssum.x;
+      slots[par][2] = ssum.y;
+      slots[par][3] = xt;
+    }
+    ptx::cluster_sync();
+    if (tid < 32) {
+      // Lane i fetches CTA i's partials; lane 0 combines them in rank order.
+      float pm = -INFINITY, ps = 0.f, px = 0.f, pt = 0.f;
+      if ((uint32_t)tid < csize) {
+        uint32_t a = ptx::mapa(ptx::smem_u32(&slots[par][0]), (uint32_t)tid);
+        pm = ptx::ld_dsmem_f32(a);
+        ps = ptx::ld_dsmem_f32(a + 4);
+        px = ptx::ld_dsmem_f32(a + 8);
+        pt = ptx::ld_dsmem_f32(a + 12);
+      }
+      float M = pm;
+      for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+      float S = 0.f, SX = 0.f, XT = 0.f;
+      for (uint32_t i = 0; i < csize; ++i) {
+        float mi = __shfl_sync(0xffffffffu, pm, i);
+        float si = __shfl_sync(0xffffffffu, ps, i);
+        float xi = __shfl_sync(0xffffffffu, px, i);
+        float ti = __shfl_sync(0xffffffffu, pt, i);
+        if (mi != -INFINITY) S += si * fexp<T>(mi - M);
+        SX += xi;
+        XT += ti;
+      }
+      if (tid == 0) {
+        stats[0] = M + logf(S);
+        stats[1] = SX;
+        stats[2] = XT;
+      }
+    }
+    __syncthreads();
+    const float lse = stats[0];
+    const bool ignored = (t == ignore_index);
+    const bool invalid = !ignored && (t < 0 || t >= n_cols);
+    if (crank == 0 && tid == 0) {
+      float loss = lse - stats[2];
+      if (lsm > 0.f) loss = (1.0f - lsm) * loss + lsm * (lse - stats[1] / (float)n_cols);
+      if (ignored) loss = 0.f;
+      if (invalid || poisoned) loss = __int_as_float(0x7fc00000);
+      loss_rows[row] = loss;
+      if (invalid) atomicExch(err, 1);
+    }
+
+    // Pass 3: gradient of this slice, straight from shared memory.
+    T* dst = grad + row * gstride + c0;
+    const float hit = 1.0f - lsm;
+    const float zero_or_nan = (invalid || poisoned) ? __int_as_float(0x7fc00000) : 0.f;
+    if (ignored || invalid || poisoned) {
+      const T z = Elt<T>::from_f(zero_or_nan);
+      if (gvec) {
+        Vec16<T> zz;
+#pragma unroll
+        for (int e = 0; e < VN; ++e) zz.e[e] = z;
+        for (int v = tid; v < nvec; v += kCeThreads) st_stream(dst + v * VN, zz);
+        for (int i = nvec * VN + tid; i < my_len; i += kCeThreads) dst[i] = z;
+      } else {
+        for (int i = tid; i < my_len; i += kCeThreads) dst[i] = z;
+      }
+    } else {
+      const int64_t tl = t - c0;  // target position inside this slice (may be outside)
+      if (gvec) {
+        for (int v = tid; v < nvec; v += kCeThreads) {
+          Vec16<T> p, o;
+          p.u = reinterpret_cast<const uint4*>(buf)[v];
+#pragma unroll
+          for (int e = 0; e < VN; ++e) {
+            float g = fexp<T>(Elt<T>::to_f(p.e[e]) - lse) - smooth;
+            if ((int64_t)(v * VN + e) == tl) g -= hit;
+            o.e[e] = Elt<T>::from_f(g * inv_nv);
+          }
+          st_stream(dst + v * VN, o);
+        }
+        for (int i = nvec * VN + tid; i < my_len; i += kCeThreads) {
+          float g = fexp<T>(Elt<T>::to_f(buf[i]) - lse) - smooth;
+          if ((int64_t)i == tl) g -= hit;
+          dst[i] = Elt<T>::from_f(g * inv_nv);
+        }
+      } else {
+        for (int i = tid; i < my_len; i += kCeThreads) {
+          float g = fexp<T>(Elt<T>::to_f(buf[i]) - lse) - smooth;
+          if ((int64_t)i == tl) g -= hit;
+          dst[i] = Elt<T>::from_f(g * inv_nv);
+        }
+      }
+    }
+    __syncthreads();  // slice buffer is free for the next row's copy
+  }
+  ptx::cluster_sync();  // no CTA leaves while a peer may still read its slots
+}
+
+// Fallback for rows longer than the cluster path holds: one CTA per row, three sweeps.
+template <typename T>
+__global__ void __launch_bounds__(kCeThreads) ce_generic_kernel(
+    const T* __restrict__ logits, int64_t lstride, T* grad, int64_t gstride,
+    const int64_t* __restrict__ targets, int64_t n_rows, int64_t n_cols, int64_t ignore_index,
+    float lsm, const int* __restrict__ n_valid_p, float* __restrict__ loss_rows,
+    int* __restrict__ err) {
+  __shared__ float red[64];
+  const float inv_nv = 1.0f / (float)(*n_valid_p);
+  const float smooth = lsm / (float)n_cols;
+  for (int64_t row = blockIdx.x; row < n_rows; row += gridDim.x) {
+    const T* src = logits + row * lstride;
+    const int64_t t = targets[row];
+    float m = -INFINITY;
+    for (int64_t i = threadIdx.x; i < n_cols; i += kCeThreads) m = fmaxf(m, Elt<T>::to_f(src[i]));
+    m = block_max(m, red);
+    float s = 0.f, sx = 0.f;
+    for (int64_t i = threadIdx.x; i < n_cols; i += kCeThreads) {
+      float x = Elt<T>::to_f(src[i]);
+      if (m != -INFINITY) s += fexp<T>(x - m);
+      sx += x;
+    }
+    float2 ss = block_sum2(s, sx, red);
+    const float lse = m + logf(ss.x);
+    const bool ignored = t == ignore_index;
+    const bool invalid = !ignored && (t < 0 || t >= n_cols);
+    if (threadIdx.x == 0) {
+      float loss = invalid ? 0.f : lse - Elt<T>::to_f(src[ignored ? 0 : t]);
+      if (lsm > 0.f) loss = (1.0f - lsm) * loss + lsm * (lse - ss.y / (float)n_cols);
+      if (ignored) loss = 0.f;
+      if (invalid) {
+        loss = __int_as_float(0x7fc00000);
+        atomicExch(err, 1);
+      }
+      loss_rows[row] = loss;
+    }
+    T* dst = grad + row * gstride;
+    for (int64_t i = threadIdx.x; i < n_cols; i += kCeThreads) {
+      float g;
+      if (invalid) g = __int_as_float(0x7fc00000);
+      else if (ignored) g = 0.f;
+      else {
+        g = fexp<T>(Elt<T>::to_f(src[i]) - lse) - smooth;
+        if (i == t) g -= 1.0f - lsm;
+        g *= inv_nv;
+      }
+      dst[i] = Elt<T>::from_f(g);
+    }
+    __syncthreads();  // all reads of this row done before a possible in-place overwrite
+  }
+}
+
+template <typename T>
+__global__ void ce_scale_kernel(T* grad, int64_t gstride, int64_t n_rows, int64_t n_cols,
+                                const float* __restrict__ go, int vec) {
+  const float s = *go;
+  if (s == 1.0f) return;
+  constexpr int VN = 16 / sizeof(T);
+  if (vec) {  // contiguous, aligned: flat 16-byte packets
+    const int64_t nv = n_rows * n_cols / VN;
+    for (int64_t v = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; v < nv;
+         v += (int64_t)gridDim.x * blockDim.x) {
+      Vec16<T> p = ld_stream(grad + v * VN);
+#pragma unroll
+      for (int e = 0; e < VN; ++e) p.e[e] = Elt<T>::from_f(Elt<T>::to_f(p.e[e]) * s);
+      st_stream(grad + v * VN, p);
+    }
+    for (int64_t i = nv * VN + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n_rows * n_cols;
+         i += (int64_t)gridDim.x * blockDim.x)
+      grad[i] = Elt<T>::from_f(Elt<T>::to_f(grad[i]) * s);
+    return;
+  }
+  for (int64_t r = blockIdx.x; r < n_rows; r += gridDim.x)
+    for (int64_t c = threadIdx.x; c < n_cols; c += blockDim.x)
+      grad[r * gstride + c] = Elt<T>::from_f(Elt<T>::to_f(grad[r * gstride + c]) * s);
+}
+
+template <typename T>
+int fwd_t(const void* logits, int64_t ls, void* grad, int64_t gs, const int64_t* targets,
+          int64_t n_rows, int64_t n_cols, int64_t ignore, float lsm, float* loss_rows,
+          float* loss, int* n_valid, int* err, cudaStream_t st) {
+  const T* lp = static_cast<const T*>(logits);
+  T* gp = static_cast<T*>(grad);
+  ce_prologue<<<1, 1024, 0, st>>>(targets, n_rows, ignore, n_valid, err);
+  int s0 = launch_status("fk_ce_fwd(prologue)");
+  if (s0 != FK_OK) return s0;
+  if (n_rows > 0) {
+    constexpr int VN = 16 / sizeof(T);
+    int C = 1;
+    auto slice = [&](int c) {
+      int64_t per = (n_cols + c - 1) / c;
+      return ((per + VN - 1) / VN) * VN;
+    };
+    while (C < 8 && slice(C) * (int64_t)sizeof(T) > kMaxClusterBytes) C <<= 1;
+    const int64_t chunk = slice(C);
+    if (chunk * (int64_t)sizeof(T) <= kMaxSliceBytes) {
+      const int smem = (int)(chunk * sizeof(T));
+      auto kern = ce_cluster_kernel<T>;
+      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+      cudaLaunchConfig_t cfg = {};
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeClusterDimension;
+      attr[0].val.clusterDim.x = C;
+      attr[0].val.clusterDim.y = 1;
+      attr[0].val.clusterDim.z = 1;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      cfg.blockDim = dim3(kCeThreads);
+      cfg.dynamicSmemBytes = smem;
+      cfg.stream = st;
+      int max_clusters = 0;
+      cfg.gridDim = dim3(C * num_sms());
+      if (cudaOccupancyMaxActiveClusters(&max_clusters, kern, &cfg) != cudaSuccess ||
+          max_clusters < 1) {
+        cudaGetLastError();
+        max_clusters = num_sms() / C;
+        if (max_clusters < 1) max_clusters = 1;
+      }
+      int64_t nclu = n_rows < max_clusters ? n_rows : max_clusters;
+      cfg.gridDim = dim3((unsigned)(nclu * C));
+      const int bulk = aligned16(lp) && ((ls * (int64_t)sizeof(T)) % 16 == 0);
+      const int gvec = aligned16(gp) && ((gs * (int64_t)sizeof(T)) % 16 == 0);
+      cudaError_t e = cudaLaunchKernelEx(&cfg, kern, lp, ls, gp, gs, targets, n_rows, (int)n_cols,
+                                         ignore, lsm, (const int*)n_valid, loss_rows, err,
+                                         (int)chunk, bulk, gvec);
+      if (e != cudaSuccess) return fail(FK_ERR_LAUNCH, "fk_ce_fwd: %s", cudaGetErrorString(e));
+    } else {
+      int64_t g = n_rows < (int64_t)num_sms() * 4 ? n_rows : (int64_t)num_sms() * 4;
+      ce_generic_kernel<T><<<(int)g, kCeThreads, 0, st>>>(lp, ls, gp, gs, targets, n_rows, n_cols,
+                                                         ignore, lsm, n_valid, loss_rows, err);
+      int s1 = launch_status("fk_ce_fwd(generic)");
+      if (s1 != FK_OK) return s1;
+    }
+  }
+  ce_finalize<<<1, 1024, 0, st>>>(loss_rows, n_rows, n_valid, loss);
+  return launch_status("fk_ce_fwd(finalize)");
+}
+
+}  // namespace
+}  // namespace fk
+
+extern "C" int fk_ce_fwd(const void* logits, int64_t row_stride, void* grad,
+                         int64_t grad_row_stride, const int64_t* targets, int64_t n_rows,
+                         int64_t n_cols, int64_t ignore_index, float label_smoothing, int dtype,
+                         float* loss_rows, float* loss, int* n_valid, int* err_flag,
+                         void* stream) {
+  FK_CHECK_ARG(n_rows >= 0 && n_cols >= 1, "fk_ce_fwd: bad shape [%lld, %lld]",
+               (long long)n_rows, (long long)n_cols);
+  FK_CHECK_ARG(n_cols < (int64_t)1 << 31, "fk_ce_fwd: n_cols too large");
+  FK_CHECK_ARG(loss && n_valid && err_flag, "fk_ce_fwd: null pointer");
+  FK_CHECK_ARG(n_rows == 0 || (logits && grad && targets && loss_rows),
+               "fk_ce_fwd: null pointer");
+  FK_CHECK_ARG(row_stride >= n_cols && grad_row_stride >= n_cols, "fk_ce_fwd: stride < n_cols");
+  FK_CHECK_ARG(label_smoothing >= 0.f && label_smoothing <= 1.f,
+               "fk_ce_fwd: label_smoothing outside [0, 1]");
+  FK_DISPATCH_DTYPE(dtype, return fk::fwd_t<scalar_t>(logits, row_stride, grad, grad_row_stride,
+                                                      targets, n_rows, n_cols, ignore_index,
+                                                      label_smoothing, loss_rows, loss, n_valid,
+                                                      err_flag, fk::as_stream(stream)));
+  return FK_OK;
+}
+
+extern "C" int fk_ce_bwd_scale(void* grad, int64_t grad_row_stride, int64_t n_rows,
+                               int64_t n_cols, const float* grad_output, int dtype,
+                               void* stream) {
+  FK_CHECK_ARG(n_rows >= 0 && n_cols >= 0, "fk_ce_bwd_scale: negative shape");
+  if (n_rows == 0 || n_cols == 0) return FK_OK;
+  FK_CHECK_ARG(grad && grad_output, "fk_ce_bwd_scale: null pointer");
+  FK_CHECK_ARG(grad_row_stride >= n_cols, "fk_ce_bwd_scale: stride < n_cols");
+  cudaStream_t st = fk::as_stream(stream);
+  FK_DISPATCH_DTYPE(dtype, {
+    const int vec = fk::aligned16(grad) && grad_row_stride == n_cols;
+    int grid = fk::num_sms() * 8;
+    fk::ce_scale_kernel<scalar_t><<<grid, 256, 0, st>>>(static_cast<scalar_t*>(grad),
+                                                        grad_row_stride, n_rows, n_cols,
+                                                        grad_output, vec);
+  });
+  return fk::launch_status("fk_ce_bwd_scale");
+}

@@ -1,0 +1,439 @@
+// RMSNorm forward/backward (fp32 accumulation, reference rmsnorm.py:20-71).
+//
+// Register path (the fast one): persistent CTAs walk rows r = blockIdx.x, += gridDim.x.
+// A CTA of T threads covers one row with VPT 16-byte packets per thread; the packet
+// index of (thread t, slot j) is j*T + t, so every slot is one fully coalesced sweep of
+// the row.  The weight slice a thread needs is loaded once into registers and reused
+// for every row the CTA visits.  The row's sum of squares is a warp-shuffle reduce plus
+// one shared-memory exchange (double-buffered by row parity, so one __syncthreads per
+// row).  The next row's packets are requested before the current row's reduction, so
+// a CTA always has loads in flight.
+//
+// Backward: the same walk; dx is written per row and the weight gradient
+// sum_r dy*x*rstd accumulates in fp32 registers owned by the thread for its fixed
+// columns.  At the end each CTA writes its partial row to the workspace and a second
+// kernel reduces the G partial rows in a fixed order (deterministic, no atomics).
+//
+// Generic path: any cols / alignment, scalar element loops re-reading the row.
+#include "common.cuh"
+
+namespace fk {
+namespace {
+
+template <typename W>
+__device__ __forceinline__ float load_w(const void* w, int64_t c) {
+  return Elt<W>::to_f(static_cast<const W*>(w)[c]);
+}
+
+__device__ __forceinline__ float block_sum(float v, float* red /*[32]*/, int nwarps) {
+  v = warp_sum(v);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  float s = 0.f;
+  for (int i = 0; i < nwarps; ++i) s += red[i];  // fixed order: deterministic
+  return s;
+}
+
+// ------------------------------------------------------------------ forward (regs) ----
+template <typename T, typename W, int VPT>
+__global__ void __launch_bounds__(512) rmsnorm_fwd_reg(const T* __restrict__ x, int64_t xs,
+                                                        const void* __restrict__ w,
+                                                        T* __restrict__ y, int64_t ys,
+                                                        float* __restrict__ rstd, int64_t rows,
+                                                        int cols, float eps) {
+  using V = Vec16<T>;
+  constexpr int N = V::N;
+  __shared__ float red[2][32];
+  const int T_ = blockDim.x, tid = threadIdx.x, nwarps = T_ >> 5;
+  const int nvec = cols / N;
+  float wr[VPT][N];
+#pragma unroll
+  for (int j = 0; j < VPT; ++j) {
+    int v = j * T_ + tid;
+#pragma unroll
+    for (int e = 0; e < N; ++e) wr[j][e] = (v < nvec) ? load_w<W>(w, (int64_t)v * N + e) : 0.f;
+  }
+  const float inv_cols = 1.0f / (float)cols;
+  int64_t r = blockIdx.x;
+  V cur[VPT];
+  if (r < rows) {
+#pragma unroll
+    for (int j = 0; j < VPT; ++j) {
+      int v = j * T_ + tid;
+      if (v < nvec) cur[j] = ld_stream(x + r * xs + (int64_t)v * N);
+      else cur[j].u = make_uint4(0, 0, 0, 0);
+    }
+  }
+  int parity = 0;
+  for (; r < rows; r += gridDim.x, parity ^= 1) {
+    const int64_t rn = r + gridDim.x;
+    V nxt[VPT];
+#pragma unroll
+    for (int j = 0; j < VPT; ++j) {
+      int v = j * T_ + tid;
+      if (rn < rows && v < nvec) nxt[j] = ld_stream(x + rn * xs + (int64_t)v * N);
+      else nxt[j].u = make_uint4(0, 0, 0, 0);
+    }
+    float ss = 0.f;
+#pragma unroll
+    for (int j = 0; j < VPT; ++j)
+#pragma unroll
+      for (int e = 0; e < N; ++e) {
+        float f = Elt<T>::to_f(cur[j].e[e]);
+        ss = fmaf(f, f, ss);
+      }
+    float tot = block_sum(ss, red[parity], nwarps);
+    float rs = rsqrtf(tot * inv_cols + eps);
+    if (tid == 0) rstd[r] = rs;
+#pragma unroll
+    for (int j = 0; j < VPT; ++j) {
+      int v = j * T_ + tid;
+      if (v < nvec) {
+        V o;
+#pragma unroll
+        for (int e = 0; e < N; ++e) o.e[e] = Elt<T>::from_f(Elt<T>::to_f(cur[j].e[e]) * rs * wr[j][e]);
+        st_stream(y + r * ys + (int64_t)v * N, o);
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < VPT; ++j) cur[j] = nxt[j];
+  }
+}
+
+// ------------------------------------------------------------------ backward (regs) ---
+template <typename T, typename W, int VPT>
+__global__ void __launch_bounds__(512) rmsnorm_bwd_reg(const T* __restrict__ dy,
+                                                        const T* __restrict__ x,
+                                                        const void* __restrict__ w,
+                                                        const float* __restrict__ rstd,
+                                                        T* __restrict__ dx,
+                                                        float* __restrict__ part, int64_t rows,
+                                                        int cols) {
+  using V = Vec16<T>;
+  constexpr int N = V::N;
+  __shared__ float red[2][32];
+  const int T_ = blockDim.x, tid = threadIdx.x, nwarps = T_ >> 5;
+  const int nvec = cols / N;
+  float wr[VPT][N], acc[VPT][N];
+#pragma unroll
+  for (int j = 0; j < VPT; ++j) {
+    int v = j * T_ + tid;
+#pragma unroll
+    for (int e = 0; e < N; ++e) {
+      wr[j][e] = (v < nvec) ? load_w<W>(w, (int64_t)v * N + e) : 0.f;
+      acc[j][e] = 0.f;
+    }
+  }
+  const float inv_cols = 1.0f / (float)cols;
+  int64_t r = blockIdx.x;
+  V cdy[VPT], cx[VPT];
+  if (r < rows) {
+#pragma unroll
+    for (int j = 0; j < VPT; ++j) {
+      int v = j * T_ + tid;
+      if (v < nvec) {
+        cdy[j] = ld_stream(dy + r * cols + (int64_t)v * N);
+        cx[j] = ld_stream(x + r * cols + (int64_t)v * N);
+      } else {
+        cdy[j].u = make_uint4(0, 0, 0, 0);
+        cx[j].u = make_uint4(0, 0, 0, 0);
+      }
+    }
+  }
+  int parity = 0;
+  for (; r < rows; r += gridDim.x, parity ^= 1) {
+    const int64_t rn = r + gridDim.x;
+    V ndy[VPT], nx[VPT];
+#pragma unroll
+    for (int j = 0; j < VPT; ++j) {
+      int v = j * T_ + tid;
+      if (rn < rows && v < nvec) {
+        ndy[j] = ld_stream(dy + rn * cols + (int64_t)v * N);
+        nx[j] = ld_stream(x + rn * cols + (int64_t)v * N);
+      } else {
+        ndy[j].u = make_uint4(0, 0, 0, 0);
+        nx[j].u = make_uint4(0, 0, 0, 0);
+      }
+    }
+    const float rs = __ldg(rstd + r);
+    float dot = 0.f;
+#pragma unroll
+    for (int j = 0; j < VPT; ++j)
+#pragma unroll
+      for (int e = 0; e < N; ++e) {
+        float d = Elt<T>::to_f(cdy[j].e[e]), xv = Elt<T>::to_f(cx[j].e[e]);
+        dot = fmaf(wr[j][e] * d, xv, dot);
+        acc[j][e] = fmaf(d * xv, rs, acc[j][e]);
+      }
+    const float tot = block_sum(dot, red[parity], nwarps);
+    const float c2 = rs * rs * rs * (tot * inv_cols);
+#pragma unroll
+    for (int j = 0; j < VPT; ++j) {
+      int v = j * T_ + tid;
+      if (v < nvec) {
+        V o;
+#pragma unroll
+        for (int e = 0; e < N; ++e) {
+          float d = Elt<T>::to_f(cdy[j].e[e]), xv = Elt<T>::to_f(cx[j].e[e]);
+          o.e[e] = Elt<T>::from_f(rs * (wr[j][e] * d) - xv * c2);
+        }
+        st_stream(dx + r * cols + (int64_t)v * N, o);
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < VPT; ++j) {
+      cdy[j] = ndy[j];
+      cx[j] = nx[j];
+    }
+  }
+  float* prow = part + (int64_t)blockIdx.x * cols;
+#pragma unroll
+  for (int j = 0; j < VPT; ++j) {
+    int v = j * T_ + tid;
+    if (v < nvec) {
+#pragma unroll
+      for (int e = 0; e < N; e += 4)
+        *reinterpret_cast<float4*>(prow + (int64_t)v * N + e) =
+            make_float4(acc[j][e], acc[j][e + 1], acc[j][e + 2], acc[j][e + 3]);
+    }
+  }
+}
+
+// ------------------------------------------------------------------ generic path ------
+template <typename T, typename W>
+__global__ void rmsnorm_fwd_generic(const T* __restrict__ x, int64_t xs, const void* __restrict__ w,
+                                    T* __restrict__ y, int64_t ys, float* __restrict__ rstd,
+                                    int64_t rows, int64_t cols, float eps) {
+  __shared__ float red[2][32];
+  const int nwarps = blockDim.x >> 5;
+  int parity = 0;
+  for (int64_t r = blockIdx.x; r < rows; r += gridDim.x, parity ^= 1) {
+    const T* xr = x + r * xs;
+    float ss = 0.f;
+    for (int64_t c = threadIdx.x; c < cols; c += blockDim.x) {
+      float f = Elt<T>::to_f(xr[c]);
+      ss = fmaf(f, f, ss);
+    }
+    float rs = rsqrtf(block_sum(ss, red[parity], nwarps) / (float)cols + eps);
+    if (threadIdx.x == 0) rstd[r] = rs;
+    for (int64_t c = threadIdx.x; c < cols; c += blockDim.x)
+      y[r * ys + c] = Elt<T>::from_f(Elt<T>::to_f(xr[c]) * rs * load_w<W>(w, c));
+  }
+}
+
+template <typename T, typename W>
+__global__ void rmsnorm_bwd_generic(const T* __restrict__ dy, const T* __restrict__ x,
+                                    const void* __restrict__ w, const float* __restrict__ rstd,
+                                    T* __restrict__ dx, float* __restrict__ part, int64_t rows,
+                                    int64_t cols) {
+  __shared__ float red[2][32];
+  const int nwarps = blockDim.x >> 5;
+  float* prow = part + (int64_t)blockIdx.x * cols;
+  for (int64_t c = threadIdx.x; c < cols; c += blockDim.x) prow[c] = 0.f;
+  int parity = 0;
+  for (int64_t r = blockIdx.x; r < rows; r += gridDim.x, parity ^= 1) {
+    const T* dyr = dy + r * cols;
+    const T* xr = x + r * cols;
+    const float rs = rstd[r];
+    float dot = 0.f;
+    for (int64_t c = threadIdx.x; c < cols; c += blockDim.x) {
+      float d = Elt<T>::to_f(dyr[c]), xv = Elt<T>::to_f(xr[c]);
+      dot = fmaf(load_w<W>(w, c) * d, xv, dot);
+      prow[c] = fmaf(d * xv, rs, prow[c]);  // each column owned by one thread
+    }
+    const float c2 = rs * rs * rs * (block_sum(dot, red[parity], nwarps) / (float)cols);
+    for (int64_t c = threadIdx.x; c < cols; c += blockDim.x) {
+      float d = Elt<T>::to_f(dyr[c]), xv = Elt<T>::to_f(xr[c]);
+      dx[r * cols + c] = Elt<T>::from_f(rs * (load_w<W>(w, c) * d) - xv * c2);
+    }
+  }
+}
+
+// dw[c] = sum_{g < G} part[g][c], fixed order, then cast to W.
+template <typename W>
+__global__ void rmsnorm_dw_reduce(const float* __restrict__ part, int G, int64_t cols,
+                                  W* __restrict__ dw) {
+  for (int64_t c = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; c < cols;
+       c += (int64_t)gridDim.x * blockDim.x) {
+    float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+    int g = 0;
+    for (; g + 3 < G; g += 4) {
+      s0 += part[(int64_t)g * cols + c];
+      s1 += part[(int64_t)(g + 1) * cols + c];
+      s2 += part[(int64_t)(g + 2) * cols + c];
+      s3 += part[(int64_t)(g + 3) * cols + c];
+    }
+    for (; g < G; ++g) s0 += part[(int64_t)g * cols + c];
+    dw[c] = Elt<W>::from_f((s0 + s1) + (s2 + s3));
+  }
+}
+
+// ------------------------------------------------------------------ launch planning ---
+struct Plan {
+  bool reg;     // register path usable
+  int threads;  // CTA size
+  int vpt;      // packets per thread (register path)
+};
+
+// Register path: 16-byte aligned rows with cols a multiple of the packet width and at
+// most kMaxVpt packets per thread (4 forward, 2 backward, so nothing spills at the
+// 128-register budget a 512-thread CTA allows).
+inline Plan plan_rows(int64_t cols, int esize, bool aligned, bool bwd) {
+  Plan p{false, 256, 0};
+  const int per = 16 / esize;
+  const int64_t nvec = cols / per;
+  const int max_vpt = bwd ? 2 : 4;
+  if (aligned && cols % per == 0 && nvec >= 1 && nvec <= 512 * max_vpt) {
+    int64_t t = nvec < 512 ? ((nvec + 31) / 32) * 32 : 512;
+    int64_t need = (nvec + t - 1) / t;
+    int v = 1;
+    while (v < need) v <<= 1;
+    p.reg = true;
+    p.threads = (int)t;
+    p.vpt = v;
+  }
+  return p;
+}
+
+// Persistent grid: resident CTAs per SM (occupancy of the actual kernel, capped at 8)
+// times the SM count, never more than rows.  kMaxGridPerSm bounds the workspace.
+constexpr int kMaxGridPerSm = 8;
+template <typename K>
+inline int persistent_grid(K kernel, int threads, int64_t rows) {
+  int per_sm = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, 0) != cudaSuccess ||
+      per_sm < 1)
+    per_sm = 1;
+  if (per_sm > kMaxGridPerSm) per_sm = kMaxGridPerSm;
+  int64_t g = (int64_t)num_sms() * per_sm;
+  if (g > rows) g = rows;
+  return (int)(g < 1 ? 1 : g);
+}
+
+template <typename T, typename W>
+int fwd_t(const void* x, int64_t xs, const void* w, void* y, int64_t ys, float* rstd,
+          int64_t rows, int64_t cols, float eps, cudaStream_t s) {
+  const bool al = aligned16(x) && aligned16(y) && (xs * (int64_t)sizeof(T)) % 16 == 0 &&
+                  (ys * (int64_t)sizeof(T)) % 16 == 0;
+  Plan p = plan_rows(cols, sizeof(T), al, false);
+  const T* xp = static_cast<const T*>(x);
+  T* yp = static_cast<T*>(y);
+  if (p.reg) {
+    switch (p.vpt) {
+#define FK_CASE(V)                                                                       \
+  case V: {                                                                              \
+    auto k = rmsnorm_fwd_reg<T, W, V>;                                                   \
+    k<<<persistent_grid(k, p.threads, rows), p.threads, 0, s>>>(xp, xs, w, yp, ys, rstd, \
+                                                                rows, (int)cols, eps);   \
+    break;                                                                               \
+  }
+      FK_CASE(1) FK_CASE(2) FK_CASE(4)
+#undef FK_CASE
+    }
+  } else {
+    auto k = rmsnorm_fwd_generic<T, W>;
+    k<<<persistent_grid(k, 256, rows), 256, 0, s>>>(xp, xs, w, yp, ys, rstd, rows, cols, eps);
+  }
+  return launch_status("fk_rmsnorm_fwd");
+}
+
+template <typename T, typename W>
+int bwd_t(const void* dy, const void* x, const void* w, const float* rstd, void* dx, void* dw,
+          float* part, int64_t rows, int64_t cols, cudaStream_t s) {
+  const bool al = aligned16(dy) && aligned16(x) && aligned16(dx);
+  Plan p = plan_rows(cols, sizeof(T), al, true);
+  const T* dyp = static_cast<const T*>(dy);
+  const T* xp = static_cast<const T*>(x);
+  T* dxp = static_cast<T*>(dx);
+  int grid = 1;
+  if (p.reg) {
+    switch (p.vpt) {
+#define FK_CASE(V)                                                                      \
+  case V: {                                                                             \
+    auto k = rmsnorm_bwd_reg<T, W, V>;                                                  \
+    grid = persistent_grid(k, p.threads, rows);                                         \
+    k<<<grid, p.threads, 0, s>>>(dyp, xp, w, rstd, dxp, part, rows, (int)cols);         \
+    break;                                                                              \
+  }
+      FK_CASE(1) FK_CASE(2)
+#undef FK_CASE
+    }
+  } else {
+    auto k = rmsnorm_bwd_generic<T, W>;
+    grid = persistent_grid(k, 256, rows);
+    k<<<grid, 256, 0, s>>>(dyp, xp, w, rstd, dxp, part, rows, cols);
+  }
+  int st = launch_status("fk_rmsnorm_bwd");
+  if (st != FK_OK) return st;
+  int rgrid = (int)((cols + 255) / 256);
+  if (rgrid > num_sms() * 4) rgrid = num_sms() * 4;
+  rmsnorm_dw_reduce<W><<<rgrid, 256, 0, s>>>(part, grid, cols, static_cast<W*>(dw));
+  return launch_status("fk_rmsnorm_bwd(dw reduce)");
+}
+
+}  // namespace
+
+// Upper bound of the backward grid (one fp32 partial row per CTA), valid for every
+// dtype and path: min(rows, SMs * kMaxGridPerSm) rows of cols floats.
+size_t rmsnorm_bwd_ws_bytes(int64_t rows, int64_t cols) {
+  int64_t g = (int64_t)num_sms() * kMaxGridPerSm;
+  if (g > rows) g = rows;
+  return (size_t)g * (size_t)cols * sizeof(float);
+}
+
+}  // namespace fk
+
+#define FK_DISPATCH_W(wd, ...)                                          \
+  switch (wd) {                                                         \
+    case FK_F32: { using wt = float; __VA_ARGS__; break; }              \
+    case FK_F16: { using wt = __half; __VA_ARGS__; break; }             \
+    case FK_BF16: { using wt = __nv_bfloat16; __VA_ARGS__; break; }     \
+    default: return ::fk::fail(FK_ERR_INVALID_ARG, "bad weight dtype %d", (int)(wd)); \
+  }
+
+extern "C" int fk_rmsnorm_fwd(const void* x, int64_t x_row_stride, const void* weight,
+                              int w_dtype, void* y, int64_t y_row_stride, float* rstd,
+                              int64_t rows, int64_t cols, float eps, int dtype, void* stream) {
+  FK_CHECK_ARG(rows >= 0 && cols >= 0, "fk_rmsnorm_fwd: negative shape");
+  if (rows == 0) return FK_OK;
+  FK_CHECK_ARG(cols > 0, "fk_rmsnorm_fwd: cols == 0");
+  FK_CHECK_ARG(x && weight && y && rstd, "fk_rmsnorm_fwd: null pointer");
+  FK_CHECK_ARG(x_row_stride >= cols && y_row_stride >= cols, "fk_rmsnorm_fwd: row stride < cols");
+  FK_DISPATCH_DTYPE(dtype, FK_DISPATCH_W(w_dtype, return fk::fwd_t<scalar_t, wt>(
+                                                      x, x_row_stride, weight, y, y_row_stride,
+                                                      rstd, rows, cols, eps,
+                                                      fk::as_stream(stream))));
+  return FK_OK;
+}
+
+extern "C" int fk_rmsnorm_bwd_workspace_size(int64_t rows, int64_t cols, size_t* bytes) {
+  FK_CHECK_ARG(bytes != nullptr, "fk_rmsnorm_bwd_workspace_size: null output");
+  FK_CHECK_ARG(rows >= 0 && cols >= 0, "fk_rmsnorm_bwd_workspace_size: negative shape");
+  *bytes = (rows == 0 || cols == 0) ? 0 : fk::rmsnorm_bwd_ws_bytes(rows, cols);
+  return FK_OK;
+}
+
+extern "C" int fk_rmsnorm_bwd(const void* dy, const void* x, const void* weight, int w_dtype,
+                              const float* rstd, void* dx, void* dw, void* workspace,
+                              size_t workspace_bytes, int64_t rows, int64_t cols, int dtype,
+                              void* stream) {
+  FK_CHECK_ARG(rows >= 0 && cols >= 0, "fk_rmsnorm_bwd: negative shape");
+  if (cols == 0) return FK_OK;
+  FK_CHECK_ARG(dw && weight, "fk_rmsnorm_bwd: null pointer");
+  if (rows == 0) {
+    // Empty batch: dw is all zeros.
+    cudaMemsetAsync(dw, 0, (size_t)cols * fk::dtype_size(w_dtype), fk::as_stream(stream));
+    return fk::launch_status("fk_rmsnorm_bwd(zero dw)");
+  }
+  FK_CHECK_ARG(dy && x && rstd && dx, "fk_rmsnorm_bwd: null pointer");
+  size_t need = fk::rmsnorm_bwd_ws_bytes(rows, cols);
+  if (workspace == nullptr || workspace_bytes < need || !fk::aligned16(workspace))
+    return fk::fail(FK_ERR_WORKSPACE, "fk_rmsnorm_bwd: need %zu aligned workspace bytes, got %zu",
+                    need, workspace_bytes);
+  FK_DISPATCH_DTYPE(dtype, FK_DISPATCH_W(w_dtype, return fk::bwd_t<scalar_t, wt>(
+                                                      dy, x, weight, rstd, dx, dw,
+                                                      static_cast<float*>(workspace), rows, cols,
+                                                      fk::as_stream(stream))));
+  return FK_OK;
+}

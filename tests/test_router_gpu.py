@@ -1,0 +1,128 @@
+"""Router kernels vs the oracle: indices bit-exact and in rank order (exact logit, ties to
+the lower expert index), weights atol 1e-6 rtol 1e-5, dlogits atol 1e-5 rtol 1e-4.
+Cases follow the reference's router tests (tests/test_moe_routing_v2.py,
+tests/test_moe_imbalance.py) plus ties, signed zeros and NaN."""
+import pytest
+import torch
+
+import fusedkernels_b200 as fk
+from oracle import route_bwd_oracle, route_oracle
+from conftest import gen
+
+pytestmark = pytest.mark.gpu
+
+
+def run(logits, k, dw=None):
+    lg = logits.cuda().requires_grad_(dw is not None)
+    w, idx = fk.fused_moe_route_v2(lg, k)
+    dl = None
+    if dw is not None:
+        w.backward(dw.cuda())
+        dl = lg.grad.float().cpu()
+    return w.detach().cpu(), idx.cpu(), dl
+
+
+def check(logits, k, with_bwd=True, seed=0):
+    dw = torch.randn(logits.shape[0], k, generator=gen(seed + 100)) if with_bwd else None
+    w, idx, dl = run(logits, k, dw)
+    rw, ridx = route_oracle(logits, k)
+    assert idx.dtype == torch.int64
+    bad = (idx != ridx).any(dim=1).nonzero()
+    assert bad.numel() == 0, f"{bad.numel()} rows differ, first {bad[:3].tolist()}"
+    torch.testing.assert_close(w, rw, atol=1e-6, rtol=1e-5, equal_nan=True)
+    if with_bwd and logits.dtype == torch.float32:
+        rdl = route_bwd_oracle(logits, k, dw)
+        torch.testing.assert_close(dl, rdl, atol=1e-5, rtol=1e-4)
+    return w, idx
+
+
+CASES = [(8, 2), (16, 4), (64, 8), (128, 16), (64, 2), (128, 8), (32, 4), (256, 8), (128, 32),
+         (4, 4), (1, 1), (3, 2), (100, 7), (200, 40), (128, 128), (64, 64), (256, 256)]
+
+
+@pytest.mark.parametrize("E,k", CASES)
+def test_router_fp32_matches_oracle(E, k):
+    logits = torch.randn(1024, E, generator=gen(E * 1000 + k))
+    check(logits, k)
+
+
+@pytest.mark.parametrize("E,k", [(8, 2), (64, 8), (128, 8), (128, 16)])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_router_16bit_ties_bit_exact(E, k, dtype):
+    """16-bit logits tie often; the lower expert index must win every tie."""
+    logits = torch.randn(4096, E, generator=gen(11)).to(dtype)
+    w, idx = check(logits, k, with_bwd=False)
+    assert idx.shape == (4096, k)
+
+
+def test_router_integer_logits_many_ties():
+    logits = torch.randint(-2, 3, (2048, 64), generator=gen(12)).float()
+    check(logits, 8)
+
+
+def test_router_signed_zero_and_nan():
+    logits = torch.zeros(4, 8)
+    logits[0, 3] = -0.0
+    logits[1] = torch.tensor([-0.0, 0.0, -0.0, 0.0, -1.0, -1.0, 1.0, -0.0])
+    logits[2, 5] = float("nan")
+    logits[3] = torch.tensor([float("-inf")] * 6 + [0.5, float("inf")])
+    w, idx, _ = run(logits, 3)
+    rw, ridx = route_oracle(logits, 3)
+    assert torch.equal(idx, ridx)
+    torch.testing.assert_close(w, rw, equal_nan=True)
+    assert idx[1].tolist() == [6, 0, 1] and idx[2, 0].item() == 5
+
+
+@pytest.mark.parametrize("E,k,skew", [(64, 8, 8.0), (128, 16, 8.0), (128, 32, 12.0)])
+def test_router_skewed_logits(E, k, skew):
+    """tests/test_moe_imbalance.py:22-53: per-expert bias of +-skew."""
+    G = gen(0)
+    bias = (torch.rand(E, generator=G) - 0.5) * 2 * skew
+    logits = torch.randn(2048, E, generator=G) + bias
+    check(logits, k)
+
+
+def test_router_saturated_logits():
+    """tests/test_moe_imbalance.py:56-77: two saturated columns (+-50)."""
+    logits = torch.randn(1024, 64, generator=gen(0)) * 2.0
+    logits[:, 0] = 50.0
+    logits[:, 1] = -50.0
+    check(logits, 8)
+
+
+def test_router_weights_sum_to_one():
+    w, _, _ = run(torch.randn(512, 32, generator=gen(1)), 4)
+    torch.testing.assert_close(w.sum(-1), torch.ones(512), atol=1e-6, rtol=0)
+
+
+def test_router_strided_rows():
+    base = torch.randn(300, 80, generator=gen(13))
+    logits = base[:, 3:67]  # row stride 80, 64 experts
+    w, idx, _ = run(logits, 8)
+    rw, ridx = route_oracle(logits.contiguous(), 8)
+    assert torch.equal(idx, ridx)
+
+
+def test_router_matches_reference_golden(golden):
+    for E, k in [(8, 2), (64, 2), (64, 8), (128, 8), (128, 16)]:
+        p = f"router_E{E}_k{k}_"
+        w, idx, dl = run(torch.from_numpy(golden[p + "logits"]), k,
+                         torch.from_numpy(golden[p + "dw"]))
+        assert torch.equal(idx, torch.from_numpy(golden[p + "idx"]).long())
+        torch.testing.assert_close(w, torch.from_numpy(golden[p + "w"]), atol=1e-6, rtol=1e-5)
+        torch.testing.assert_close(dl, torch.from_numpy(golden[p + "dlogits"]), atol=1e-6, rtol=1e-5)
+
+
+def test_router_large_batch_bit_exact():
+    """N=131072 rows (examples/moe_router_sweep_n.py's largest N), E=128, k=8, bf16."""
+    logits = torch.randn(131072, 128, generator=gen(14)).bfloat16()
+    _, idx, _ = run(logits, 8)
+    _, ridx = route_oracle(logits, 8)
+    assert torch.equal(idx, ridx)
+
+
+def test_router_deterministic():
+    logits = torch.randn(1024, 128, generator=gen(15))
+    outs = [run(logits, 32, torch.ones(1024, 32)) for _ in range(5)]
+    for o in outs[1:]:
+        assert all(torch.equal(a, b) for a, b in zip(o, outs[0]))
