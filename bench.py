@@ -120,8 +120,29 @@ def gen(seed):
     return torch.Generator().manual_seed(seed)
 
 
+def cur_stream():
+    return torch.cuda.current_stream().cuda_stream
+
+
+def make_graph(fn, inner):
+    """Capture `inner` back-to-back calls of fn (C-ABI launches) in a CUDA graph."""
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        fn()
+    torch.cuda.current_stream().wait_stream(side)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for _ in range(inner):
+            fn()
+    torch.cuda.synchronize()
+    return g
+
+
 # ----------------------------------------------------------------------------- workloads --
 class Workload:
+    graph_inner = 1
     name = ""
     metric = ""
     unit = ""
@@ -158,7 +179,6 @@ class RMSNorm(Workload):
         self.rstd = torch.empty(R, dtype=torch.float32, device=dev)
         wsb = _lib.rmsnorm_bwd_workspace_bytes(R, C, dev)
         self.ws = torch.empty(wsb, dtype=torch.uint8, device=dev)
-        self.stream = torch.cuda.current_stream(dev).cuda_stream
         e = 2
         self.fwd_bytes = R * C * e * 2 + C * 4 + R * 4
         self.bwd_bytes = R * C * e * 3 + C * 4 * 2 + R * 4
@@ -167,12 +187,12 @@ class RMSNorm(Workload):
     def fwd(self):
         self.lib.call("fk_rmsnorm_fwd", self.x.data_ptr(), self.cols, self.w.data_ptr(), 0,
                       self.y.data_ptr(), self.cols, self.rstd.data_ptr(), self.rows, self.cols,
-                      1e-6, 2, self.stream)
+                      1e-6, 2, cur_stream())
 
     def bwd(self):
         self.lib.call("fk_rmsnorm_bwd", self.dy.data_ptr(), self.x.data_ptr(), self.w.data_ptr(),
                       0, self.rstd.data_ptr(), self.dx.data_ptr(), self.dw.data_ptr(),
-                      self.ws.data_ptr(), self.ws.numel(), self.rows, self.cols, 2, self.stream)
+                      self.ws.data_ptr(), self.ws.numel(), self.rows, self.cols, 2, cur_stream())
 
     def step(self):
         self.fwd()
@@ -248,18 +268,17 @@ class SwiGLU(Workload):
         self.dg = torch.empty_like(self.g)
         self.du = torch.empty_like(self.g)
         self.n = self.g.numel()
-        self.stream = torch.cuda.current_stream(dev).cuda_stream
         self.fwd_bytes = self.n * 2 * 3
         self.bwd_bytes = self.n * 2 * 5
         self.dev = dev
 
     def fwd(self):
         self.lib.call("fk_swiglu_fwd", self.g.data_ptr(), self.u.data_ptr(), self.out.data_ptr(),
-                      self.n, 2, self.stream)
+                      self.n, 2, cur_stream())
 
     def bwd(self):
         self.lib.call("fk_swiglu_bwd", self.d.data_ptr(), self.g.data_ptr(), self.u.data_ptr(),
-                      self.dg.data_ptr(), self.du.data_ptr(), self.n, 2, self.stream)
+                      self.dg.data_ptr(), self.du.data_ptr(), self.n, 2, cur_stream())
 
     def step(self):
         self.fwd()
@@ -331,7 +350,6 @@ class CrossEntropy(Workload):
         self.loss = torch.empty((), dtype=torch.float32, device=dev)
         self.flags = torch.zeros(2, dtype=torch.int32, device=dev)
         self.go = torch.ones((), dtype=torch.float32, device=dev)
-        self.stream = torch.cuda.current_stream(dev).cuda_stream
         self.bytes = self.rows * self.cols * 2 * 2 + self.rows * 8
         self.dev = dev
 
@@ -339,11 +357,11 @@ class CrossEntropy(Workload):
         self.lib.call("fk_ce_fwd", self.x.data_ptr(), self.cols, self.x.data_ptr(), self.cols,
                       self.t.data_ptr(), self.rows, self.cols, -100, 0.0, 2,
                       self.loss_rows.data_ptr(), self.loss.data_ptr(), self.flags.data_ptr(),
-                      self.flags.data_ptr() + 4, self.stream)
+                      self.flags.data_ptr() + 4, cur_stream())
 
     def bwd(self):
         self.lib.call("fk_ce_bwd_scale", self.x.data_ptr(), self.cols, self.rows, self.cols,
-                      self.go.data_ptr(), 2, self.stream)
+                      self.go.data_ptr(), 2, cur_stream())
 
     def step(self):
         self.fwd()
@@ -401,6 +419,7 @@ class Router(Workload):
     unit = "tokens/s"
     dtype = "f32"
     E, k = 64, 2
+    graph_inner = 20
 
     def __init__(self, rows=4096):
         self.rows = rows
@@ -416,18 +435,17 @@ class Router(Workload):
         self.w = torch.empty(self.rows, self.k, device=dev)
         self.idx = torch.empty(self.rows, self.k, dtype=torch.int64, device=dev)
         self.dl = torch.empty(self.rows, self.E, device=dev)
-        self.stream = torch.cuda.current_stream(dev).cuda_stream
         self.fwd_bytes = self.rows * (self.E * 4 + self.k * 12)
         self.bwd_bytes = self.rows * (self.k * 16 + self.E * 4)
         self.dev = dev
 
     def fwd(self):
         self.lib.call("fk_router_fwd", self.l.data_ptr(), self.E, 0, self.rows, self.E, self.k,
-                      self.w.data_ptr(), self.idx.data_ptr(), self.stream)
+                      self.w.data_ptr(), self.idx.data_ptr(), cur_stream())
 
     def bwd(self):
         self.lib.call("fk_router_bwd", self.dwt.data_ptr(), self.w.data_ptr(), self.idx.data_ptr(),
-                      self.dl.data_ptr(), self.rows, self.E, self.k, self.stream)
+                      self.dl.data_ptr(), self.rows, self.E, self.k, cur_stream())
 
     def step(self):
         self.fwd()
@@ -515,36 +533,45 @@ def run_ours(args):
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                              device_id=dev)
     wl = Router(args.router_rows) if args.workload == "router" else WORKLOADS[args.workload]()
+    if args.rows and hasattr(wl, "rows") and args.workload != "router":
+        wl.rows = args.rows
     wl.setup(dev)
     stream = torch.cuda.current_stream(dev)
     pk = peaks()
 
+    # The timed steps replay a CUDA graph of the step's C-ABI launches (`inner` steps per
+    # graph for launch-latency-bound workloads), so the number is device time.
+    inner = wl.graph_inner
+    graph = make_graph(wl.step, inner)
+    reps = max(1, args.steps // inner) if inner > 1 else args.steps
     for _ in range(args.warmup):
-        wl.step()
+        graph.replay()
     torch.cuda.synchronize(dev)
     barrier()
     with ClockSampler(dev.index) as clk:
         t0 = time.perf_counter()
-        ms = time_device(wl.step, args.steps, stream)
-        # keep sampling for at least ~1 s of load so the clock record is meaningful
+        ms = time_device(graph.replay, reps, stream)
+        # keep the GPU loaded for ~1 s so the clock record has samples under load
         extra = 0
-        while time.perf_counter() - t0 < 1.0 and extra < 10000:
-            wl.step()
+        while time.perf_counter() - t0 < 1.0 and extra < 20000:
+            graph.replay()
             extra += 1
         torch.cuda.synchronize(dev)
     barrier()
     ms = max_over_ranks(ms, dev)
-    ms_per_step = ms / args.steps
+    n_steps = reps * inner
+    ms_per_step = ms / n_steps
     value = wl.units_per_step() * world / (ms_per_step / 1e3)
 
     # Dominant kernel: per-launch duration with CUDA events on the launching stream.
     kern = []
     for name, fn, nbytes in wl.kernels():
+        kg = make_graph(fn, inner)
         for _ in range(3):
-            fn()
+            kg.replay()
         torch.cuda.synchronize(dev)
-        reps = max(args.steps, 10)
-        kms = time_device(fn, reps, stream) / reps
+        kreps = max(args.steps, 10)
+        kms = time_device(kg.replay, kreps, stream) / (kreps * inner)
         kern.append({"kernel": name, "ms": round(kms, 5), "bytes": nbytes,
                      "gbs": round(nbytes / (kms / 1e3) / 1e9, 1)})
     dom = max(kern, key=lambda k: k["ms"] if wl.name != "router" else k["bytes"])
@@ -574,11 +601,12 @@ def run_ours(args):
 
     if rank == 0:
         out = {"metric": wl.metric, "value": value, "unit": wl.unit, "n_gpus": world,
-               "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 5),
+               "steps": n_steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 5),
                "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
                "dtype": wl.dtype, "data": "synthetic (seeded torch.randn, shapes of the workload)",
                "config": wl.config(), "roofline": roof, "kernels": kern, "cpu_baseline": cpu,
-               "e2e": e2e, "gpu_launches": wl.launches_per_step * args.steps,
+               "e2e": e2e, "gpu_launches": wl.launches_per_step * n_steps,
+               "timing": f"CUDA graph of {inner} step(s) replayed {reps}x, CUDA events",
                "clocks": clk.summary()}
         print(json.dumps(out), flush=True)
     if torch.distributed.is_initialized():
@@ -674,6 +702,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="rmsnorm")
     ap.add_argument("--router-rows", type=int, default=4096)
+    ap.add_argument("--rows", type=int, default=0,
+                    help="override the row count of rmsnorm/swiglu/ce (profiling runs only)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3:

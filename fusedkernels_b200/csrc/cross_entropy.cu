@@ -3,18 +3,20 @@
 // HBM traffic is one read of the logits and one write of the gradient.  A row of V
 // logits (250.5 KiB for V=128256 bf16) is larger than one SM's shared memory, so a
 // thread-block CLUSTER of C CTAs (C <= 8) owns a row: CTA c bulk-copies (cp.async.bulk,
-// mbarrier-completed) its 1/C slice of the row into shared memory, reduces it to
-// (max, sum exp, sum x, target logit), and the C partials are exchanged through
-// distributed shared memory.  Every CTA combines the partials in rank order (so all CTAs
-// hold bit-identical statistics), then writes the gradient of its slice straight from
-// shared memory.  Nothing is re-read from HBM.  Clusters are persistent and walk rows
-// r = cluster_id, += n_clusters; partial slots are double-buffered by row parity so one
-// cluster barrier per row suffices.
+// mbarrier-completed) its 1/C slice of the row into shared memory, reduces it in ONE pass
+// to (max, sum exp, sum x) with an online rescale, and the C partials (plus the target
+// logit) are exchanged through distributed shared memory.  Every CTA combines the
+// partials in rank order (so all CTAs hold bit-identical statistics), then writes the
+// gradient of its slice straight from shared memory.  Nothing is re-read from HBM.
+// Clusters are persistent and walk rows r = cluster_id, += n_clusters; each CTA holds two
+// slice buffers and copies row r+1 while it works on row r; partial slots are
+// double-buffered by row parity so one cluster barrier per row suffices.  Exponentials
+// of 16-bit inputs are single ex2 instructions with log2(e) folded into an FMA.
 //
 // The mean-reduction scale 1/n_valid is folded into the gradient write (n_valid comes
 // from a one-CTA prologue that counts non-ignored targets), and the scalar loss is a
 // fixed-order reduction of the per-row losses (deterministic).  Rows longer than
-// 8 x 200 KiB fall back to a three-sweep kernel that re-reads the row from global memory.
+// 8 x 108 KiB fall back to a three-sweep kernel that re-reads the row from global memory.
 #include "common.cuh"
 #include "ptx.cuh"
 
@@ -22,8 +24,8 @@ namespace fk {
 namespace {
 
 constexpr int kCeThreads = 256;
-constexpr int kMaxClusterBytes = 40 * 1024;   // target slice size per CTA
-constexpr int kMaxSliceBytes = 200 * 1024;    // hard cap (dynamic shared memory)
+constexpr int kMaxClusterBytes = 32 * 1024;   // target slice size per CTA
+constexpr int kMaxSliceBytes = 108 * 1024;    // hard cap: two slices in shared memory
 constexpr uint32_t kBulkPiece = 32 * 1024;    // bytes per cp.async.bulk instruction
 
 template <typename T>
@@ -93,6 +95,92 @@ __device__ __forceinline__ float2 block_sum2(float a, float b, float* red) {
   return make_float2(sa, sb);
 }
 
+// Online (max, sum of exp) accumulation in the base-2 domain: values are kept as
+// x*log2(e), so every exponential is one ex2 (16-bit inputs) or expf (fp32 inputs).
+struct Online {
+  float m;   // running max of x
+  float s;   // sum exp(x - m)
+  float sx;  // sum x
+};
+
+__device__ __forceinline__ float ex2f(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+constexpr float kLog2e = 1.4426950408889634f;
+
+template <typename T>
+__device__ __forceinline__ float exp_shift(float x, float m) {  // exp(x - m)
+  return ex2f(fmaf(x, kLog2e, -m * kLog2e));
+}
+template <>
+__device__ __forceinline__ float exp_shift<float>(float x, float m) {
+  return expf(x - m);
+}
+
+template <typename T>
+__device__ __forceinline__ Online combine(Online a, Online b) {
+  Online r;
+  r.m = fmaxf(a.m, b.m);
+  r.sx = a.sx + b.sx;
+  if (r.m == -INFINITY) {
+    r.s = 0.f;
+  } else {
+    r.s = (a.m == -INFINITY ? 0.f : a.s * exp_shift<T>(a.m, r.m)) +
+          (b.m == -INFINITY ? 0.f : b.s * exp_shift<T>(b.m, r.m));
+  }
+  return r;
+}
+
+template <typename T>
+__device__ __forceinline__ void online_add_packet(Online& o, const Vec16<T>& p) {
+  constexpr int VN = Vec16<T>::N;
+  float x[VN];
+  float pm = -INFINITY;
+#pragma unroll
+  for (int e = 0; e < VN; ++e) {
+    x[e] = Elt<T>::to_f(p.e[e]);
+    pm = fmaxf(pm, x[e]);
+    o.sx += x[e];
+  }
+  const float mn = fmaxf(o.m, pm);
+  if (mn == -INFINITY) return;
+  if (o.m != mn) {
+    o.s = (o.m == -INFINITY) ? 0.f : o.s * exp_shift<T>(o.m, mn);
+    o.m = mn;
+  }
+  float acc = 0.f;
+#pragma unroll
+  for (int e = 0; e < VN; ++e) acc += exp_shift<T>(x[e], mn);
+  o.s += acc;
+}
+
+template <typename T>
+__device__ __forceinline__ void online_add_scalar(Online& o, float x) {
+  o.sx += x;
+  const float mn = fmaxf(o.m, x);
+  if (mn == -INFINITY) return;
+  if (o.m != mn) {
+    o.s = (o.m == -INFINITY) ? 0.f : o.s * exp_shift<T>(o.m, mn);
+    o.m = mn;
+  }
+  o.s += exp_shift<T>(x, mn);
+}
+
+template <typename T>
+__device__ __forceinline__ Online warp_combine(Online o) {
+#pragma unroll
+  for (int d = 16; d > 0; d >>= 1) {
+    Online b;
+    b.m = __shfl_xor_sync(0xffffffffu, o.m, d);
+    b.s = __shfl_xor_sync(0xffffffffu, o.s, d);
+    b.sx = __shfl_xor_sync(0xffffffffu, o.sx, d);
+    o = combine<T>(o, b);
+  }
+  return o;
+}
+
 template <typename T>
 __global__ void __launch_bounds__(kCeThreads) ce_cluster_kernel(
     const T* __restrict__ logits, int64_t lstride, T* grad, int64_t gstride,
@@ -101,13 +189,14 @@ __global__ void __launch_bounds__(kCeThreads) ce_cluster_kernel(
     int* __restrict__ err, int chunk, int bulk, int gvec) {
   constexpr int VN = 16 / sizeof(T);
   extern __shared__ __align__(128) unsigned char smem_raw[];
-  T* buf = reinterpret_cast<T*>(smem_raw);
-  __shared__ __align__(8) uint64_t bar;
+  auto buf_of = [&](int b) { return reinterpret_cast<T*>(smem_raw + (size_t)b * chunk * sizeof(T)); };
+  __shared__ __align__(8) uint64_t full[2];
   __shared__ float slots[2][4];  // [row parity] {max, sum exp, sum x, target logit}
-  __shared__ float red[64];
-  __shared__ float stats[4];     // combined {lse, sum x, target logit, unused}
+  __shared__ float wred[3][8];
+  __shared__ float stats[4];     // combined {lse, sum x, target logit}
+  __shared__ int dead;
 
-  const int tid = threadIdx.x;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const uint32_t crank = ptx::cluster_ctarank();
   const uint32_t csize = ptx::cluster_nctarank();
   const int64_t c0 = (int64_t)crank * chunk;
@@ -116,78 +205,79 @@ __global__ void __launch_bounds__(kCeThreads) ce_cluster_kernel(
   if (my_len < 0) my_len = 0;
   const int bulk_len = bulk ? (my_len / VN) * VN : 0;
   const uint32_t bulk_bytes = (uint32_t)bulk_len * sizeof(T);
+  const int nvec = my_len / VN;
+
+  const int64_t row0 = ptx::cluster_id_x();
+  const int64_t rstep = ptx::nclusters_x();
+  auto issue = [&](int64_t row, int b) {
+    const unsigned char* src =
+        reinterpret_cast<const unsigned char*>(logits + row * lstride + c0);
+    unsigned char* dst = reinterpret_cast<unsigned char*>(buf_of(b));
+    ptx::fence_proxy_async_smem();
+    ptx::mbar_arrive_expect_tx(&full[b], bulk_bytes);
+    for (uint32_t off = 0; off < bulk_bytes; off += kBulkPiece) {
+      uint32_t n = bulk_bytes - off < kBulkPiece ? bulk_bytes - off : kBulkPiece;
+      ptx::bulk_g2s(dst + off, src + off, n, &full[b]);
+    }
+  };
 
   if (tid == 0) {
-    ptx::mbar_init(&bar, 1);
+    ptx::mbar_init(&full[0], 1);
+    ptx::mbar_init(&full[1], 1);
     ptx::fence_mbar_init();
+    dead = 0;
   }
   __syncthreads();
+  if (tid == 0 && bulk_len > 0 && row0 < n_rows) issue(row0, 0);
 
   const float inv_nv = 1.0f / (float)(*n_valid_p);
   const float smooth = lsm / (float)n_cols;
-  uint32_t phase = 0;
-  int par = 0;
-  for (int64_t row = ptx::cluster_id_x(); row < n_rows; row += ptx::nclusters_x(), par ^= 1) {
+  const float hit = 1.0f - lsm;
+  int it = 0;
+  for (int64_t row = row0; row < n_rows; row += rstep, ++it) {
+    const int b = it & 1;
+    const int par = it & 1;
+    T* buf = buf_of(b);
     const T* src = logits + row * lstride + c0;
-    if (tid == 0 && bulk_len > 0) {
-      ptx::fence_proxy_async_smem();
-      ptx::mbar_arrive_expect_tx(&bar, bulk_bytes);
-      for (uint32_t off = 0; off < bulk_bytes; off += kBulkPiece) {
-        uint32_t n = bulk_bytes - off < kBulkPiece ? bulk_bytes - off : kBulkPiece;
-        ptx::bulk_g2s(reinterpret_cast<unsigned char*>(buf) + off,
-                      reinterpret_cast<const unsigned char*>(src) + off, n, &bar);
+    bool poisoned = false;
+    if (bulk_len > 0) {
+      if (dead || !ptx::mbar_wait(&full[b], (uint32_t)((it >> 1) & 1))) {
+        poisoned = true;
+        if (!dead) atomicExch(err, 2);
       }
     }
     for (int i = bulk_len + tid; i < my_len; i += kCeThreads) buf[i] = src[i];
     const int64_t t = targets[row];
-    bool poisoned = false;
-    if (bulk_len > 0) {
-      if (!ptx::mbar_wait(&bar, phase)) {
-        poisoned = true;  // copy never completed: report, keep cluster barriers aligned
-        atomicExch(err, 2);
-      }
-      phase ^= 1;
-    }
     __syncthreads();
+    if (poisoned && tid == 0) dead = 1;
+    // Prefetch the next row into the other buffer (freed at the end of the last row).
+    if (tid == 0 && bulk_len > 0 && !dead && row + rstep < n_rows) issue(row + rstep, b ^ 1);
 
-    // Pass 1: slice max.  Pass 2: slice sum of exp(x - max) and sum of x.
-    const int nvec = my_len / VN;
-    float m = -INFINITY;
+    // One pass over the slice: online max / sum exp / sum x.
+    Online o{-INFINITY, 0.f, 0.f};
+    const uint4* bv = reinterpret_cast<const uint4*>(buf);
     for (int v = tid; v < nvec; v += kCeThreads) {
       Vec16<T> p;
-      p.u = reinterpret_cast<const uint4*>(buf)[v];
-#pragma unroll
-      for (int e = 0; e < VN; ++e) m = fmaxf(m, Elt<T>::to_f(p.e[e]));
+      p.u = bv[v];
+      online_add_packet<T>(o, p);
     }
-    for (int i = nvec * VN + tid; i < my_len; i += kCeThreads) m = fmaxf(m, Elt<T>::to_f(buf[i]));
-    const float mc = block_max(m, red);
-    float s = 0.f, sx = 0.f;
-    if (mc != -INFINITY) {
-      for (int v = tid; v < nvec; v += kCeThreads) {
-        Vec16<T> p;
-        p.u = reinterpret_cast<const uint4*>(buf)[v];
-#pragma unroll
-        for (int e = 0; e < VN; ++e) {
-          float x = Elt<T>::to_f(p.e[e]);
-          s += fexp<T>(x - mc);
-          sx += x;
-        }
-      }
-      for (int i = nvec * VN + tid; i < my_len; i += kCeThreads) {
-        float x = Elt<T>::to_f(buf[i]);
-        s += fexp<T>(x - mc);
-        sx += x;
-      }
-    } else {
-      for (int i = tid; i < my_len; i += kCeThreads) sx += Elt<T>::to_f(buf[i]);
+    for (int i = nvec * VN + tid; i < my_len; i += kCeThreads)
+      online_add_scalar<T>(o, Elt<T>::to_f(buf[i]));
+    o = warp_combine<T>(o);
+    if (lane == 0) {
+      wred[0][warp] = o.m;
+      wred[1][warp] = o.s;
+      wred[2][warp] = o.sx;
     }
-    const float2 ssum = block_sum2(s, sx, red);
+    __syncthreads();
     if (tid == 0) {
+      Online c{wred[0][0], wred[1][0], wred[2][0]};
+      for (int w = 1; w < kCeThreads / 32; ++w) c = combine<T>(c, Online{wred[0][w], wred[1][w], wred[2][w]});
       float xt = 0.f;
       if (t >= c0 && t < c0 + my_len) xt = Elt<T>::to_f(buf[t - c0]);
-      slots[par][0] = mc;
-      slots[par][1] = ssum.x;
-      slots[par][2] = ssum.y;
+      slots[par][0] = c.m;
+      slots[par][1] = c.s;
+      slots[par][2] = c.sx;
       slots[par][3] = xt;
     }
     ptx::cluster_sync();
@@ -201,21 +291,17 @@ __global__ void __launch_bounds__(kCeThreads) ce_cluster_kernel(
         px = ptx::ld_dsmem_f32(a + 8);
         pt = ptx::ld_dsmem_f32(a + 12);
       }
-      float M = pm;
-      for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
-      float S = 0.f, SX = 0.f, XT = 0.f;
+      Online c{-INFINITY, 0.f, 0.f};
+      float XT = 0.f;
       for (uint32_t i = 0; i < csize; ++i) {
-        float mi = __shfl_sync(0xffffffffu, pm, i);
-        float si = __shfl_sync(0xffffffffu, ps, i);
-        float xi = __shfl_sync(0xffffffffu, px, i);
-        float ti = __shfl_sync(0xffffffffu, pt, i);
-        if (mi != -INFINITY) S += si * fexp<T>(mi - M);
-        SX += xi;
-        XT += ti;
+        Online q{__shfl_sync(0xffffffffu, pm, i), __shfl_sync(0xffffffffu, ps, i),
+                 __shfl_sync(0xffffffffu, px, i)};
+        c = combine<T>(c, q);
+        XT += __shfl_sync(0xffffffffu, pt, i);
       }
       if (tid == 0) {
-        stats[0] = M + logf(S);
-        stats[1] = SX;
+        stats[0] = c.m + logf(c.s);
+        stats[1] = c.sx;
         stats[2] = XT;
       }
     }
@@ -232,12 +318,10 @@ __global__ void __launch_bounds__(kCeThreads) ce_cluster_kernel(
       if (invalid) atomicExch(err, 1);
     }
 
-    // Pass 3: gradient of this slice, straight from shared memory.
+    // Gradient of this slice, straight from shared memory.
     T* dst = grad + row * gstride + c0;
-    const float hit = 1.0f - lsm;
-    const float zero_or_nan = (invalid || poisoned) ? __int_as_float(0x7fc00000) : 0.f;
     if (ignored || invalid || poisoned) {
-      const T z = Elt<T>::from_f(zero_or_nan);
+      const T z = Elt<T>::from_f((invalid || poisoned) ? __int_as_float(0x7fc00000) : 0.f);
       if (gvec) {
         Vec16<T> zz;
 #pragma unroll
@@ -249,32 +333,41 @@ __global__ void __launch_bounds__(kCeThreads) ce_cluster_kernel(
       }
     } else {
       const int64_t tl = t - c0;  // target position inside this slice (may be outside)
+      const float sub = smooth * inv_nv;
+      const float hsub = hit * inv_nv;
+      // exp(x - lse) * inv_nv == 2^(x*log2e - (lse*log2e - log2(inv_nv)))
+      const float cexp = lse * kLog2e - log2f(inv_nv);
+      auto gval = [&](float x) -> float {
+        if constexpr (sizeof(T) == 4) return expf(x - lse) * inv_nv - sub;
+        else return ex2f(fmaf(x, kLog2e, -cexp)) - sub;
+      };
       if (gvec) {
+        const int tv = (tl >= 0 && tl < nvec * VN) ? (int)(tl / VN) : -1;
         for (int v = tid; v < nvec; v += kCeThreads) {
           Vec16<T> p, o;
-          p.u = reinterpret_cast<const uint4*>(buf)[v];
+          p.u = bv[v];
+          float g[VN];
 #pragma unroll
-          for (int e = 0; e < VN; ++e) {
-            float g = fexp<T>(Elt<T>::to_f(p.e[e]) - lse) - smooth;
-            if ((int64_t)(v * VN + e) == tl) g -= hit;
-            o.e[e] = Elt<T>::from_f(g * inv_nv);
-          }
+          for (int e = 0; e < VN; ++e) g[e] = gval(Elt<T>::to_f(p.e[e]));
+          if (v == tv) g[tl - (int64_t)v * VN] -= hsub;
+#pragma unroll
+          for (int e = 0; e < VN; ++e) o.e[e] = Elt<T>::from_f(g[e]);
           st_stream(dst + v * VN, o);
         }
         for (int i = nvec * VN + tid; i < my_len; i += kCeThreads) {
-          float g = fexp<T>(Elt<T>::to_f(buf[i]) - lse) - smooth;
-          if ((int64_t)i == tl) g -= hit;
-          dst[i] = Elt<T>::from_f(g * inv_nv);
+          float g = gval(Elt<T>::to_f(buf[i]));
+          if ((int64_t)i == tl) g -= hsub;
+          dst[i] = Elt<T>::from_f(g);
         }
       } else {
         for (int i = tid; i < my_len; i += kCeThreads) {
-          float g = fexp<T>(Elt<T>::to_f(buf[i]) - lse) - smooth;
-          if ((int64_t)i == tl) g -= hit;
-          dst[i] = Elt<T>::from_f(g * inv_nv);
+          float g = gval(Elt<T>::to_f(buf[i]));
+          if ((int64_t)i == tl) g -= hsub;
+          dst[i] = Elt<T>::from_f(g);
         }
       }
     }
-    __syncthreads();  // slice buffer is free for the next row's copy
+    __syncthreads();  // this buffer is free for the copy issued two rows from now
   }
   ptx::cluster_sync();  // no CTA leaves while a peer may still read its slots
 }
@@ -375,7 +468,7 @@ int fwd_t(const void* logits, int64_t ls, void* grad, int64_t gs, const int64_t*
     while (C < 8 && slice(C) * (int64_t)sizeof(T) > kMaxClusterBytes) C <<= 1;
     const int64_t chunk = slice(C);
     if (chunk * (int64_t)sizeof(T) <= kMaxSliceBytes) {
-      const int smem = (int)(chunk * sizeof(T));
+      const int smem = (int)(2 * chunk * sizeof(T));
       auto kern = ce_cluster_kernel<T>;
       cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
       cudaLaunchConfig_t cfg = {};

@@ -6,8 +6,8 @@
 // the row.  The weight slice a thread needs is loaded once into registers and reused
 // for every row the CTA visits.  The row's sum of squares is a warp-shuffle reduce plus
 // one shared-memory exchange (double-buffered by row parity, so one __syncthreads per
-// row).  The next row's packets are requested before the current row's reduction, so
-// a CTA always has loads in flight.
+// row).  Each CTA keeps PF rows of loads in flight (register ring, refilled as soon as
+// a row is consumed), so a CTA always has loads outstanding across its reductions.
 //
 // Backward: the same walk; dx is written per row and the weight gradient
 // sum_r dy*x*rstd accumulates in fp32 registers owned by the thread for its fixed
@@ -16,6 +16,7 @@
 //
 // Generic path: any cols / alignment, scalar element loops re-reading the row.
 #include "common.cuh"
+#include "ptx.cuh"
 
 namespace fk {
 namespace {
@@ -36,7 +37,9 @@ __device__ __forceinline__ float block_sum(float v, float* red /*[32]*/, int nwa
 }
 
 // ------------------------------------------------------------------ forward (regs) ----
-template <typename T, typename W, int VPT>
+// PF rows are in flight per CTA: the slot consumed for row r is refilled with row
+// r + PF*grid right after use, so PF-1 rows of loads overlap every reduction.
+template <typename T, typename W, int VPT, int PF>
 __global__ void __launch_bounds__(512) rmsnorm_fwd_reg(const T* __restrict__ x, int64_t xs,
                                                         const void* __restrict__ w,
                                                         T* __restrict__ y, int64_t ys,
@@ -47,6 +50,7 @@ __global__ void __launch_bounds__(512) rmsnorm_fwd_reg(const T* __restrict__ x, 
   __shared__ float red[2][32];
   const int T_ = blockDim.x, tid = threadIdx.x, nwarps = T_ >> 5;
   const int nvec = cols / N;
+  const int64_t G = gridDim.x;
   float wr[VPT][N];
 #pragma unroll
   for (int j = 0; j < VPT; ++j) {
@@ -55,54 +59,53 @@ __global__ void __launch_bounds__(512) rmsnorm_fwd_reg(const T* __restrict__ x, 
     for (int e = 0; e < N; ++e) wr[j][e] = (v < nvec) ? load_w<W>(w, (int64_t)v * N + e) : 0.f;
   }
   const float inv_cols = 1.0f / (float)cols;
-  int64_t r = blockIdx.x;
-  V cur[VPT];
-  if (r < rows) {
+  V slot[PF][VPT];
+  auto load_row = [&](V (&dst)[VPT], int64_t r) {
 #pragma unroll
     for (int j = 0; j < VPT; ++j) {
       int v = j * T_ + tid;
-      if (v < nvec) cur[j] = ld_stream(x + r * xs + (int64_t)v * N);
-      else cur[j].u = make_uint4(0, 0, 0, 0);
+      if (r < rows && v < nvec) dst[j] = ld_stream(x + r * xs + (int64_t)v * N);
+      else dst[j].u = make_uint4(0, 0, 0, 0);
     }
-  }
+  };
+#pragma unroll
+  for (int q = 0; q < PF; ++q) load_row(slot[q], blockIdx.x + q * G);
   int parity = 0;
-  for (; r < rows; r += gridDim.x, parity ^= 1) {
-    const int64_t rn = r + gridDim.x;
-    V nxt[VPT];
+  for (int64_t base = blockIdx.x; base < rows; base += PF * G) {
 #pragma unroll
-    for (int j = 0; j < VPT; ++j) {
-      int v = j * T_ + tid;
-      if (rn < rows && v < nvec) nxt[j] = ld_stream(x + rn * xs + (int64_t)v * N);
-      else nxt[j].u = make_uint4(0, 0, 0, 0);
-    }
-    float ss = 0.f;
+    for (int q = 0; q < PF; ++q) {
+      const int64_t r = base + q * G;
+      if (r >= rows) break;
+      float ss = 0.f;
 #pragma unroll
-    for (int j = 0; j < VPT; ++j)
+      for (int j = 0; j < VPT; ++j)
 #pragma unroll
-      for (int e = 0; e < N; ++e) {
-        float f = Elt<T>::to_f(cur[j].e[e]);
-        ss = fmaf(f, f, ss);
+        for (int e = 0; e < N; ++e) {
+          float f = Elt<T>::to_f(slot[q][j].e[e]);
+          ss = fmaf(f, f, ss);
+        }
+      const float tot = block_sum(ss, red[parity], nwarps);
+      parity ^= 1;
+      const float rs = rsqrtf(tot * inv_cols + eps);
+      if (tid == 0) rstd[r] = rs;
+#pragma unroll
+      for (int j = 0; j < VPT; ++j) {
+        int v = j * T_ + tid;
+        if (v < nvec) {
+          V o;
+#pragma unroll
+          for (int e = 0; e < N; ++e)
+            o.e[e] = Elt<T>::from_f(Elt<T>::to_f(slot[q][j].e[e]) * rs * wr[j][e]);
+          st_stream(y + r * ys + (int64_t)v * N, o);
+        }
       }
-    float tot = block_sum(ss, red[parity], nwarps);
-    float rs = rsqrtf(tot * inv_cols + eps);
-    if (tid == 0) rstd[r] = rs;
-#pragma unroll
-    for (int j = 0; j < VPT; ++j) {
-      int v = j * T_ + tid;
-      if (v < nvec) {
-        V o;
-#pragma unroll
-        for (int e = 0; e < N; ++e) o.e[e] = Elt<T>::from_f(Elt<T>::to_f(cur[j].e[e]) * rs * wr[j][e]);
-        st_stream(y + r * ys + (int64_t)v * N, o);
-      }
+      load_row(slot[q], r + PF * G);
     }
-#pragma unroll
-    for (int j = 0; j < VPT; ++j) cur[j] = nxt[j];
   }
 }
 
 // ------------------------------------------------------------------ backward (regs) ---
-template <typename T, typename W, int VPT>
+template <typename T, typename W, int VPT, int PF>
 __global__ void __launch_bounds__(512) rmsnorm_bwd_reg(const T* __restrict__ dy,
                                                         const T* __restrict__ x,
                                                         const void* __restrict__ w,
@@ -115,6 +118,7 @@ __global__ void __launch_bounds__(512) rmsnorm_bwd_reg(const T* __restrict__ dy,
   __shared__ float red[2][32];
   const int T_ = blockDim.x, tid = threadIdx.x, nwarps = T_ >> 5;
   const int nvec = cols / N;
+  const int64_t G = gridDim.x;
   float wr[VPT][N], acc[VPT][N];
 #pragma unroll
   for (int j = 0; j < VPT; ++j) {
@@ -126,51 +130,239 @@ __global__ void __launch_bounds__(512) rmsnorm_bwd_reg(const T* __restrict__ dy,
     }
   }
   const float inv_cols = 1.0f / (float)cols;
-  int64_t r = blockIdx.x;
-  V cdy[VPT], cx[VPT];
-  if (r < rows) {
+  V sdy[PF][VPT], sx[PF][VPT];
+  auto load_row = [&](V (&ddy)[VPT], V (&dxx)[VPT], int64_t r) {
 #pragma unroll
     for (int j = 0; j < VPT; ++j) {
       int v = j * T_ + tid;
+      if (r < rows && v < nvec) {
+        ddy[j] = ld_stream(dy + r * cols + (int64_t)v * N);
+        dxx[j] = ld_stream(x + r * cols + (int64_t)v * N);
+      } else {
+        ddy[j].u = make_uint4(0, 0, 0, 0);
+        dxx[j].u = make_uint4(0, 0, 0, 0);
+      }
+    }
+  };
+#pragma unroll
+  for (int q = 0; q < PF; ++q) load_row(sdy[q], sx[q], blockIdx.x + q * G);
+  int parity = 0;
+  for (int64_t base = blockIdx.x; base < rows; base += PF * G) {
+#pragma unroll
+    for (int q = 0; q < PF; ++q) {
+      const int64_t r = base + q * G;
+      if (r >= rows) break;
+      const float rs = __ldg(rstd + r);
+      float dot = 0.f;
+#pragma unroll
+      for (int j = 0; j < VPT; ++j)
+#pragma unroll
+        for (int e = 0; e < N; ++e) {
+          float d = Elt<T>::to_f(sdy[q][j].e[e]), xv = Elt<T>::to_f(sx[q][j].e[e]);
+          dot = fmaf(wr[j][e] * d, xv, dot);
+          acc[j][e] = fmaf(d * xv, rs, acc[j][e]);
+        }
+      const float tot = block_sum(dot, red[parity], nwarps);
+      parity ^= 1;
+      const float c2 = rs * rs * rs * (tot * inv_cols);
+#pragma unroll
+      for (int j = 0; j < VPT; ++j) {
+        int v = j * T_ + tid;
+        if (v < nvec) {
+          V o;
+#pragma unroll
+          for (int e = 0; e < N; ++e) {
+            float d = Elt<T>::to_f(sdy[q][j].e[e]), xv = Elt<T>::to_f(sx[q][j].e[e]);
+            o.e[e] = Elt<T>::from_f(rs * (wr[j][e] * d) - xv * c2);
+          }
+          st_stream(dx + r * cols + (int64_t)v * N, o);
+        }
+      }
+      load_row(sdy[q], sx[q], r + PF * G);
+    }
+  }
+  float* prow = part + (int64_t)blockIdx.x * cols;
+#pragma unroll
+  for (int j = 0; j < VPT; ++j) {
+    int v = j * T_ + tid;
+    if (v < nvec) {
+#pragma unroll
+      for (int e = 0; e < N; e += 4)
+        *reinterpret_cast<float4*>(prow + (int64_t)v * N + e) =
+            make_float4(acc[j][e], acc[j][e + 1], acc[j][e + 2], acc[j][e + 3]);
+    }
+  }
+}
+
+// ------------------------------------------------------------------ TMA ring path -----
+// Rows are staged through a ring of STAGES shared-memory buffers filled by cp.async.bulk
+// (one mbarrier per stage), so a CTA keeps up to STAGES rows of HBM reads in flight
+// without spending registers on them.  Each thread copies its packets out of the stage
+// into registers before the block reduction; the reduction's __syncthreads therefore
+// also frees the stage, and thread 0 immediately refills it with the row STAGES ahead.
+// A wait that does not complete within the bound poisons the rest of the CTA's rows
+// with NaN instead of spinning.
+constexpr int kRingThreads = 256;
+constexpr int kRingStages = 4;
+
+template <typename T>
+__device__ __forceinline__ void ring_issue(unsigned char* stage, uint64_t* bar, const T* src0,
+                                           const T* src1, uint32_t row_bytes) {
+  ptx::fence_proxy_async_smem();
+  ptx::mbar_arrive_expect_tx(bar, src1 ? 2 * row_bytes : row_bytes);
+  ptx::bulk_g2s(stage, src0, row_bytes, bar);
+  if (src1) ptx::bulk_g2s(stage + row_bytes, src1, row_bytes, bar);
+}
+
+template <typename T, typename W, int VPT>
+__global__ void __launch_bounds__(kRingThreads) rmsnorm_fwd_ring(
+    const T* __restrict__ x, int64_t xs, const void* __restrict__ w, T* __restrict__ y,
+    int64_t ys, float* __restrict__ rstd, int64_t rows, int cols, float eps) {
+  using V = Vec16<T>;
+  constexpr int N = V::N;
+  extern __shared__ __align__(128) unsigned char ring[];
+  __shared__ __align__(8) uint64_t full[kRingStages];
+  __shared__ float red[2][32];
+  __shared__ int dead;
+  const int tid = threadIdx.x;
+  const int nvec = cols / N;
+  const uint32_t row_bytes = (uint32_t)cols * sizeof(T);
+  const int64_t G = gridDim.x;
+  float wr[VPT][N];
+#pragma unroll
+  for (int j = 0; j < VPT; ++j) {
+    int v = j * kRingThreads + tid;
+#pragma unroll
+    for (int e = 0; e < N; ++e) wr[j][e] = (v < nvec) ? load_w<W>(w, (int64_t)v * N + e) : 0.f;
+  }
+  if (tid == 0) {
+    for (int q = 0; q < kRingStages; ++q) ptx::mbar_init(&full[q], 1);
+    ptx::fence_mbar_init();
+    dead = 0;
+  }
+  __syncthreads();
+  if (tid == 0)
+    for (int q = 0; q < kRingStages; ++q) {
+      const int64_t r = blockIdx.x + q * G;
+      if (r < rows) ring_issue<T>(ring + (size_t)q * row_bytes, &full[q], x + r * xs, (const T*)nullptr, row_bytes);
+    }
+  const float inv_cols = 1.0f / (float)cols;
+  int i = 0;
+  for (int64_t r = blockIdx.x; r < rows; r += G, ++i) {
+    const int q = i % kRingStages;
+    const bool ok = !dead && ptx::mbar_wait(&full[q], (uint32_t)((i / kRingStages) & 1));
+    const V* sv = reinterpret_cast<const V*>(ring + (size_t)q * row_bytes);
+    V cur[VPT];
+    float ss = 0.f;
+#pragma unroll
+    for (int j = 0; j < VPT; ++j) {
+      int v = j * kRingThreads + tid;
+      if (v < nvec) cur[j] = sv[v];
+      else cur[j].u = make_uint4(0, 0, 0, 0);
+#pragma unroll
+      for (int e = 0; e < N; ++e) {
+        float f = Elt<T>::to_f(cur[j].e[e]);
+        ss = fmaf(f, f, ss);
+      }
+    }
+    const float tot = block_sum(ss, red[i & 1], kRingThreads / 32);  // also frees stage q
+    if (tid == 0) {
+      if (!ok) dead = 1;
+      const int64_t rn = r + kRingStages * G;
+      if (!dead && rn < rows)
+        ring_issue<T>(ring + (size_t)q * row_bytes, &full[q], x + rn * xs, (const T*)nullptr, row_bytes);
+    }
+    const float rs = ok ? rsqrtf(tot * inv_cols + eps) : __int_as_float(0x7fc00000);
+    if (tid == 0) rstd[r] = rs;
+#pragma unroll
+    for (int j = 0; j < VPT; ++j) {
+      int v = j * kRingThreads + tid;
       if (v < nvec) {
-        cdy[j] = ld_stream(dy + r * cols + (int64_t)v * N);
-        cx[j] = ld_stream(x + r * cols + (int64_t)v * N);
+        V o;
+#pragma unroll
+        for (int e = 0; e < N; ++e) o.e[e] = Elt<T>::from_f(Elt<T>::to_f(cur[j].e[e]) * rs * wr[j][e]);
+        st_stream(y + r * ys + (int64_t)v * N, o);
+      }
+    }
+  }
+}
+
+template <typename T, typename W, int VPT>
+__global__ void __launch_bounds__(kRingThreads) rmsnorm_bwd_ring(
+    const T* __restrict__ dy, const T* __restrict__ x, const void* __restrict__ w,
+    const float* __restrict__ rstd, T* __restrict__ dx, float* __restrict__ part, int64_t rows,
+    int cols) {
+  using V = Vec16<T>;
+  constexpr int N = V::N;
+  extern __shared__ __align__(128) unsigned char ring[];
+  __shared__ __align__(8) uint64_t full[kRingStages];
+  __shared__ float red[2][32];
+  __shared__ int dead;
+  const int tid = threadIdx.x;
+  const int nvec = cols / N;
+  const uint32_t row_bytes = (uint32_t)cols * sizeof(T);
+  const size_t stage_bytes = 2 * (size_t)row_bytes;
+  const int64_t G = gridDim.x;
+  float wr[VPT][N], acc[VPT][N];
+#pragma unroll
+  for (int j = 0; j < VPT; ++j) {
+    int v = j * kRingThreads + tid;
+#pragma unroll
+    for (int e = 0; e < N; ++e) {
+      wr[j][e] = (v < nvec) ? load_w<W>(w, (int64_t)v * N + e) : 0.f;
+      acc[j][e] = 0.f;
+    }
+  }
+  if (tid == 0) {
+    for (int q = 0; q < kRingStages; ++q) ptx::mbar_init(&full[q], 1);
+    ptx::fence_mbar_init();
+    dead = 0;
+  }
+  __syncthreads();
+  if (tid == 0)
+    for (int q = 0; q < kRingStages; ++q) {
+      const int64_t r = blockIdx.x + q * G;
+      if (r < rows)
+        ring_issue<T>(ring + q * stage_bytes, &full[q], dy + r * cols, x + r * cols, row_bytes);
+    }
+  const float inv_cols = 1.0f / (float)cols;
+  int i = 0;
+  for (int64_t r = blockIdx.x; r < rows; r += G, ++i) {
+    const int q = i % kRingStages;
+    const bool ok = !dead && ptx::mbar_wait(&full[q], (uint32_t)((i / kRingStages) & 1));
+    const V* sdy = reinterpret_cast<const V*>(ring + q * stage_bytes);
+    const V* sx = reinterpret_cast<const V*>(ring + q * stage_bytes + row_bytes);
+    const float rs = __ldg(rstd + r);
+    V cdy[VPT], cx[VPT];
+    float dot = 0.f;
+#pragma unroll
+    for (int j = 0; j < VPT; ++j) {
+      int v = j * kRingThreads + tid;
+      if (v < nvec) {
+        cdy[j] = sdy[v];
+        cx[j] = sx[v];
       } else {
         cdy[j].u = make_uint4(0, 0, 0, 0);
         cx[j].u = make_uint4(0, 0, 0, 0);
       }
-    }
-  }
-  int parity = 0;
-  for (; r < rows; r += gridDim.x, parity ^= 1) {
-    const int64_t rn = r + gridDim.x;
-    V ndy[VPT], nx[VPT];
-#pragma unroll
-    for (int j = 0; j < VPT; ++j) {
-      int v = j * T_ + tid;
-      if (rn < rows && v < nvec) {
-        ndy[j] = ld_stream(dy + rn * cols + (int64_t)v * N);
-        nx[j] = ld_stream(x + rn * cols + (int64_t)v * N);
-      } else {
-        ndy[j].u = make_uint4(0, 0, 0, 0);
-        nx[j].u = make_uint4(0, 0, 0, 0);
-      }
-    }
-    const float rs = __ldg(rstd + r);
-    float dot = 0.f;
-#pragma unroll
-    for (int j = 0; j < VPT; ++j)
 #pragma unroll
       for (int e = 0; e < N; ++e) {
         float d = Elt<T>::to_f(cdy[j].e[e]), xv = Elt<T>::to_f(cx[j].e[e]);
         dot = fmaf(wr[j][e] * d, xv, dot);
         acc[j][e] = fmaf(d * xv, rs, acc[j][e]);
       }
-    const float tot = block_sum(dot, red[parity], nwarps);
-    const float c2 = rs * rs * rs * (tot * inv_cols);
+    }
+    const float tot = block_sum(dot, red[i & 1], kRingThreads / 32);  // also frees stage q
+    if (tid == 0) {
+      if (!ok) dead = 1;
+      const int64_t rn = r + kRingStages * G;
+      if (!dead && rn < rows)
+        ring_issue<T>(ring + q * stage_bytes, &full[q], dy + rn * cols, x + rn * cols, row_bytes);
+    }
+    const float c2 = ok ? rs * rs * rs * (tot * inv_cols) : __int_as_float(0x7fc00000);
 #pragma unroll
     for (int j = 0; j < VPT; ++j) {
-      int v = j * T_ + tid;
+      int v = j * kRingThreads + tid;
       if (v < nvec) {
         V o;
 #pragma unroll
@@ -181,16 +373,11 @@ __global__ void __launch_bounds__(512) rmsnorm_bwd_reg(const T* __restrict__ dy,
         st_stream(dx + r * cols + (int64_t)v * N, o);
       }
     }
-#pragma unroll
-    for (int j = 0; j < VPT; ++j) {
-      cdy[j] = ndy[j];
-      cx[j] = nx[j];
-    }
   }
   float* prow = part + (int64_t)blockIdx.x * cols;
 #pragma unroll
   for (int j = 0; j < VPT; ++j) {
-    int v = j * T_ + tid;
+    int v = j * kRingThreads + tid;
     if (v < nvec) {
 #pragma unroll
       for (int e = 0; e < N; e += 4)
@@ -296,13 +483,26 @@ inline Plan plan_rows(int64_t cols, int esize, bool aligned, bool bwd) {
   return p;
 }
 
+// Ring path: 16-byte aligned rows of at most 4 packets per thread (256 threads) and at
+// most 16 KiB, so four stages of (dy, x) fit in 128 KiB.  Returns VPT or 0.
+inline int ring_vpt(int64_t cols, int esize, bool aligned) {
+  const int per = 16 / esize;
+  if (!aligned || cols % per != 0 || cols * esize > 16 * 1024) return 0;
+  const int64_t nvec = cols / per;
+  const int64_t need = (nvec + kRingThreads - 1) / kRingThreads;
+  if (need <= 1) return 1;
+  if (need <= 2) return 2;
+  if (need <= 4) return 4;
+  return 0;
+}
+
 // Persistent grid: resident CTAs per SM (occupancy of the actual kernel, capped at 8)
 // times the SM count, never more than rows.  kMaxGridPerSm bounds the workspace.
 constexpr int kMaxGridPerSm = 8;
 template <typename K>
-inline int persistent_grid(K kernel, int threads, int64_t rows) {
+inline int persistent_grid(K kernel, int threads, int64_t rows, int smem = 0) {
   int per_sm = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, 0) != cudaSuccess ||
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, smem) != cudaSuccess ||
       per_sm < 1)
     per_sm = 1;
   if (per_sm > kMaxGridPerSm) per_sm = kMaxGridPerSm;
@@ -319,11 +519,26 @@ int fwd_t(const void* x, int64_t xs, const void* w, void* y, int64_t ys, float* 
   Plan p = plan_rows(cols, sizeof(T), al, false);
   const T* xp = static_cast<const T*>(x);
   T* yp = static_cast<T*>(y);
-  if (p.reg) {
+  const int rv = ring_vpt(cols, sizeof(T), al);
+  if (rv > 0) {
+    const int smem = kRingStages * (int)(cols * sizeof(T));
+    switch (rv) {
+#define FK_CASE(V)                                                                      \
+  case V: {                                                                             \
+    auto k = rmsnorm_fwd_ring<T, W, V>;                                                 \
+    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);          \
+    k<<<persistent_grid(k, kRingThreads, rows, smem), kRingThreads, smem, s>>>(         \
+        xp, xs, w, yp, ys, rstd, rows, (int)cols, eps);                                  \
+    break;                                                                              \
+  }
+      FK_CASE(1) FK_CASE(2) FK_CASE(4)
+#undef FK_CASE
+    }
+  } else if (p.reg) {
     switch (p.vpt) {
 #define FK_CASE(V)                                                                       \
   case V: {                                                                              \
-    auto k = rmsnorm_fwd_reg<T, W, V>;                                                   \
+    auto k = rmsnorm_fwd_reg<T, W, V, (V == 1 ? 4 : 2)>;                                                   \
     k<<<persistent_grid(k, p.threads, rows), p.threads, 0, s>>>(xp, xs, w, yp, ys, rstd, \
                                                                 rows, (int)cols, eps);   \
     break;                                                                               \
@@ -347,11 +562,26 @@ int bwd_t(const void* dy, const void* x, const void* w, const float* rstd, void*
   const T* xp = static_cast<const T*>(x);
   T* dxp = static_cast<T*>(dx);
   int grid = 1;
-  if (p.reg) {
+  const int rv = ring_vpt(cols, sizeof(T), al);
+  if (rv > 0) {
+    const int smem = kRingStages * 2 * (int)(cols * sizeof(T));
+    switch (rv) {
+#define FK_CASE(V)                                                                      \
+  case V: {                                                                             \
+    auto k = rmsnorm_bwd_ring<T, W, V>;                                                 \
+    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);          \
+    grid = persistent_grid(k, kRingThreads, rows, smem);                                \
+    k<<<grid, kRingThreads, smem, s>>>(dyp, xp, w, rstd, dxp, part, rows, (int)cols);     \
+    break;                                                                              \
+  }
+      FK_CASE(1) FK_CASE(2) FK_CASE(4)
+#undef FK_CASE
+    }
+  } else if (p.reg) {
     switch (p.vpt) {
 #define FK_CASE(V)                                                                      \
   case V: {                                                                             \
-    auto k = rmsnorm_bwd_reg<T, W, V>;                                                  \
+    auto k = rmsnorm_bwd_reg<T, W, V, (V == 1 ? 3 : 2)>;                                                  \
     grid = persistent_grid(k, p.threads, rows);                                         \
     k<<<grid, p.threads, 0, s>>>(dyp, xp, w, rstd, dxp, part, rows, (int)cols);         \
     break;                                                                              \

@@ -12,13 +12,14 @@
 // segment of S lanes (S = min(32, L)), V keys per lane; element i = r*S + lane.
 // E <= 32 packs 32/S rows into each warp.
 //
-// Selection ("group then merge", k <= S): each register row r (S keys across the
-// segment) is bitonic-sorted with warp shuffles, descending for even r and ascending for
-// odd r.  Then registers are merged pairwise: elementwise max of a descending and an
-// ascending run holds the top S of their union as a bitonic sequence, which a log2(S)
-// step bitonic merge sorts again.  log2(V) such levels leave the top S, sorted, in
-// register 0.  For k > S a full bitonic sort of all L keys is used (intra-lane steps
-// for distances >= S).
+// Selection ("group then merge", k <= S): runs of KP = next_pow2(k) keys are
+// bitonic-sorted with warp shuffles, then folded pairwise -- the elementwise max of a
+// descending and an ascending run holds the top KP of their union as a bitonic run,
+// which a log2(KP)-step bitonic merge sorts again -- first across the V registers of a
+// lane (no shuffles), then across lanes.  Work is O(L log^2 KP) instead of the
+// O(L log^2 L) of a full sort.  For k > S a full bitonic sort of all L keys is used.
+// Two rows are processed per warp pass when V <= 2 (independent shuffle chains), and the
+// next pass's logits are loaded before the current pass's network runs.
 //
 // Weights.  The renormalised top-k softmax equals a softmax over the k selected logits:
 // w_j = exp(x_j - m) / sum_{i in top-k} exp(x_i - m), with m the largest logit (the
@@ -64,116 +65,179 @@ __device__ __forceinline__ float seg_sum(float v) {
   return v;
 }
 
-template <typename T, int S, int V, bool FULL>
+// Bitonic merge of runs of KP lanes (distances KP/2 .. 1) toward direction `desc`.
+template <int KP>
+__device__ __forceinline__ uint64_t merge_runs(uint64_t m, int lane_s, bool desc) {
+#pragma unroll
+  for (int d = KP >> 1; d > 0; d >>= 1) m = cx_lanes(m, d, lane_s, desc);
+  return m;
+}
+
+// Top-k keys of one row held as key[V] (element i = r*S + lane_s), group-then-merge:
+//  A) bitonic-sort runs of KP = next_pow2(k) lanes inside every register;
+//  B) fold registers pairwise (elementwise max of a descending and an ascending run is
+//     the top KP of both, as a bitonic run) and re-merge, log2(V) levels, no shuffles
+//     for the max;
+//  C) fold runs across lanes the same way at distances KP, 2KP, .., S/2.
+// Run directions are chosen so every fold sees (descending, ascending) partners; the
+// result is the top KP, sorted descending, in register 0 of lanes 0..KP-1 of the segment.
+template <int S, int V, int KP>
+__device__ __forceinline__ uint64_t topk_group_merge(uint64_t (&key)[V], int lane_s) {
+  // final direction of the runs of register r after phase A / each phase-B level
+  auto lane_alt = [&](int period) { return ((lane_s / period) & 1) == 0; };
+  const bool lanes_follow = KP < S;  // phase C exists
+  // Phase A
+#pragma unroll
+  for (int size = 2; size <= KP; size <<= 1) {
+#pragma unroll
+    for (int d = size >> 1; d > 0; d >>= 1) {
+#pragma unroll
+      for (int r = 0; r < V; ++r) {
+        bool want_desc = (V > 1) ? ((r & 1) == 0) : (lanes_follow ? lane_alt(KP) : true);
+        bool natural_desc = ((lane_s & KP) == 0) || KP == S;
+        bool desc = (((lane_s & size) == 0) || size == S) != (natural_desc != want_desc);
+        if (size == KP) desc = want_desc;
+        key[r] = cx_lanes(key[r], d, lane_s, desc);
+      }
+    }
+  }
+  // Phase B
+#pragma unroll
+  for (int h = 1; h < V; h <<= 1) {
+#pragma unroll
+    for (int r = 0; r < V; r += 2 * h) {
+      uint64_t m = kmax(key[r], key[r + h]);
+      bool desc;
+      if (2 * h < V) desc = ((r / (2 * h)) & 1) == 0;
+      else desc = lanes_follow ? lane_alt(KP) : true;
+      key[r] = merge_runs<KP>(m, lane_s, desc);
+    }
+  }
+  // Phase C
+  uint64_t m = key[0];
+#pragma unroll
+  for (int d = KP; d < S; d <<= 1) {
+    m = kmax(m, shfl_xor64(m, d));
+    m = merge_runs<KP>(m, lane_s, lane_alt(2 * d));
+  }
+  return m;
+}
+
+template <typename T, int S, int V, int KP, bool FULL, int RPI>
 __global__ void __launch_bounds__(256) router_fwd_kernel(const T* __restrict__ logits,
                                                          int64_t row_stride, int64_t n_rows,
                                                          int E, int k, float* __restrict__ w_out,
                                                          int64_t* __restrict__ idx_out) {
   constexpr int L = S * V;
-  constexpr int RPW = 32 / S;  // rows per warp
+  constexpr int RPW = 32 / S;  // rows per warp per pass
   const int lane = threadIdx.x & 31;
   const int lane_s = lane % S;
   const int seg = lane / S;
   const int64_t warp_global = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int64_t n_warps = ((int64_t)gridDim.x * blockDim.x) >> 5;
-  const int64_t n_groups = (n_rows + RPW - 1) / RPW;
+  const int64_t n_groups = (n_rows + RPW * RPI - 1) / (RPW * RPI);
 
-  for (int64_t g = warp_global; g < n_groups; g += n_warps) {
-    const int64_t row = g * RPW + seg;
-    const bool row_ok = row < n_rows;
-    uint64_t key[V];
+  auto load = [&](float (&x)[RPI][V], int64_t g) {
 #pragma unroll
-    for (int r = 0; r < V; ++r) {
-      int e = r * S + lane_s;
-      key[r] = 0;
-      if (row_ok && e < E) {
-        float x = Elt<T>::to_f(logits[row * row_stride + e]);
-        key[r] = ((uint64_t)ordered_bits(x) << 32) | (uint32_t)(E - 1 - e);
+    for (int q = 0; q < RPI; ++q) {
+      const int64_t row = (g * RPI + q) * RPW + seg;
+#pragma unroll
+      for (int r = 0; r < V; ++r) {
+        const int e = r * S + lane_s;
+        x[q][r] = (g < n_groups && row < n_rows && e < E)
+                      ? Elt<T>::to_f(logits[row * row_stride + e]) : 0.f;
       }
     }
-
+  };
+  float cur[RPI][V];
+  load(cur, warp_global);
+  for (int64_t g = warp_global; g < n_groups; g += n_warps) {
+    float nxt[RPI][V];
+    load(nxt, g + n_warps);  // next group's logits in flight during this group's sort
+    uint64_t top[RPI], keyv[RPI][V];
+#pragma unroll
+    for (int q = 0; q < RPI; ++q) {
+      const int64_t row = (g * RPI + q) * RPW + seg;
+#pragma unroll
+      for (int r = 0; r < V; ++r) {
+        const int e = r * S + lane_s;
+        keyv[q][r] = (row < n_rows && e < E)
+                         ? (((uint64_t)ordered_bits(cur[q][r]) << 32) | (uint32_t)(E - 1 - e))
+                         : 0ull;
+      }
+    }
     if constexpr (!FULL) {
-      // Phase A: sort each register row; even rows descending, odd rows ascending.
 #pragma unroll
-      for (int size = 2; size <= S; size <<= 1) {
-#pragma unroll
-        for (int d = size >> 1; d > 0; d >>= 1) {
-#pragma unroll
-          for (int r = 0; r < V; ++r) {
-            bool desc = (((lane_s & size) == 0) != ((r & 1) != 0));
-            key[r] = cx_lanes(key[r], d, lane_s, desc);
-          }
-        }
-      }
-      // Phase B: pairwise max-merge of registers, keeping the top S each level.
-#pragma unroll
-      for (int h = 1; h < V; h <<= 1) {
-#pragma unroll
-        for (int r = 0; r < V; r += 2 * h) {
-          uint64_t m = kmax(key[r], key[r + h]);
-          const bool desc = ((r / (2 * h)) & 1) == 0;
-#pragma unroll
-          for (int d = S >> 1; d > 0; d >>= 1) m = cx_lanes(m, d, lane_s, desc);
-          key[r] = m;
-        }
-      }
+      for (int q = 0; q < RPI; ++q) top[q] = topk_group_merge<S, V, KP>(keyv[q], lane_s);
     } else {
-      // Full bitonic sort of L keys, descending.
+      // Full bitonic sort of L keys, descending (k > 32).
 #pragma unroll
-      for (int size = 2; size <= L; size <<= 1) {
+      for (int q = 0; q < RPI; ++q) {
 #pragma unroll
-        for (int d = size >> 1; d > 0; d >>= 1) {
-          if (d >= S) {
-            const int rd = d / S;
+        for (int size = 2; size <= L; size <<= 1) {
 #pragma unroll
-            for (int r = 0; r < V; ++r) {
-              if ((r & rd) == 0) {
+          for (int d = size >> 1; d > 0; d >>= 1) {
+            if (d >= S) {
+              const int rd = d / S;
+#pragma unroll
+              for (int r = 0; r < V; ++r) {
+                if ((r & rd) == 0) {
+                  const int i = r * S + lane_s;
+                  const bool desc = (i & size) == 0;
+                  uint64_t a = keyv[q][r], b = keyv[q][r + rd];
+                  keyv[q][r] = desc ? kmax(a, b) : kmin(a, b);
+                  keyv[q][r + rd] = desc ? kmin(a, b) : kmax(a, b);
+                }
+              }
+            } else {
+#pragma unroll
+              for (int r = 0; r < V; ++r) {
                 const int i = r * S + lane_s;
-                const bool desc = (i & size) == 0;
-                uint64_t a = key[r], b = key[r + rd];
-                key[r] = desc ? kmax(a, b) : kmin(a, b);
-                key[r + rd] = desc ? kmin(a, b) : kmax(a, b);
+                keyv[q][r] = cx_lanes(keyv[q][r], d, lane_s, (i & size) == 0);
               }
             }
-          } else {
-#pragma unroll
-            for (int r = 0; r < V; ++r) {
-              const int i = r * S + lane_s;
-              key[r] = cx_lanes(key[r], d, lane_s, (i & size) == 0);
-            }
           }
         }
+        top[q] = keyv[q][0];
       }
     }
-
-    // Top element (global max logit) sits in register 0 of segment lane 0.
-    const uint64_t top = __shfl_sync(0xffffffffu, key[0], seg * S);
-    const float m = from_ordered((uint32_t)(top >> 32));
-    constexpr int VK = FULL ? V : 1;  // registers that can hold rank < k
-    float ex[VK];
-    float s = 0.f;
 #pragma unroll
-    for (int r = 0; r < VK; ++r) {
-      const int j = r * S + lane_s;
-      ex[r] = 0.f;
-      if (j < k) {
-        ex[r] = expf(from_ordered((uint32_t)(key[r] >> 32)) - m);
-        s += ex[r];
-      }
-    }
-    s = seg_sum<S>(s);
-    if (row_ok) {
-      const float inv = 1.0f / s;
+    for (int q = 0; q < RPI; ++q) {
+      const int64_t row = (g * RPI + q) * RPW + seg;
+      // Largest logit: rank 0, register 0 of segment lane 0.
+      const uint64_t t0 = __shfl_sync(0xffffffffu, top[q], seg * S);
+      const float m = from_ordered((uint32_t)(t0 >> 32));
+      constexpr int VK = FULL ? V : 1;  // registers that can hold rank < k
+      float ex[VK];
+      uint64_t kk[VK];
+      float ssum = 0.f;
 #pragma unroll
       for (int r = 0; r < VK; ++r) {
         const int j = r * S + lane_s;
+        kk[r] = FULL ? keyv[q][r] : top[q];
+        ex[r] = 0.f;
         if (j < k) {
-          w_out[row * k + j] = ex[r] * inv;
-          idx_out[row * k + j] = (int64_t)(E - 1 - (int)(uint32_t)key[r]);
+          ex[r] = expf(from_ordered((uint32_t)(kk[r] >> 32)) - m);
+          ssum += ex[r];
+        }
+      }
+      ssum = seg_sum<S>(ssum);
+      if (row < n_rows) {
+        const float inv = 1.0f / ssum;
+#pragma unroll
+        for (int r = 0; r < VK; ++r) {
+          const int j = r * S + lane_s;
+          if (j < k) {
+            w_out[row * k + j] = ex[r] * inv;
+            idx_out[row * k + j] = (int64_t)(E - 1 - (int)(uint32_t)kk[r]);
+          }
         }
       }
     }
-    (void)L;
+#pragma unroll
+    for (int q = 0; q < RPI; ++q)
+#pragma unroll
+      for (int r = 0; r < V; ++r) cur[q][r] = nxt[q][r];
   }
 }
 
@@ -237,6 +301,34 @@ inline int warp_grid(int64_t n_groups) {
   return (int)(ctas < 1 ? 1 : ctas);
 }
 
+template <typename T, int S, int V>
+int launch_gm(const T* lp, int64_t rs, int64_t n, int E, int k, float* w, int64_t* idx,
+              cudaStream_t st) {
+  constexpr int RPI = (V <= 2) ? 2 : 1;
+  const int64_t groups = (n + (32 / S) * RPI - 1) / ((32 / S) * RPI);
+  const int grid = warp_grid(groups);
+  const int KP = pow2_at_least(k);
+#define FK_KP(KP_)                                                                          \
+  case KP_:                                                                                 \
+    router_fwd_kernel<T, S, V, (KP_ < S ? KP_ : S), false, RPI><<<grid, 256, 0, st>>>(       \
+        lp, rs, n, E, k, w, idx);                                                           \
+    break;
+  switch (KP) {
+    FK_KP(1) FK_KP(2) FK_KP(4) FK_KP(8) FK_KP(16) FK_KP(32)
+    default: return fail(FK_ERR_UNSUPPORTED, "fk_router_fwd: k=%d", k);
+  }
+#undef FK_KP
+  return FK_OK;
+}
+
+template <typename T, int V>
+int launch_full(const T* lp, int64_t rs, int64_t n, int E, int k, float* w, int64_t* idx,
+                cudaStream_t st) {
+  const int grid = warp_grid(n);
+  router_fwd_kernel<T, 32, V, 32, true, 1><<<grid, 256, 0, st>>>(lp, rs, n, E, k, w, idx);
+  return FK_OK;
+}
+
 template <typename T>
 int fwd_t(const void* logits, int64_t rs, int64_t n, int E, int k, float* w, int64_t* idx,
           cudaStream_t st) {
@@ -244,34 +336,30 @@ int fwd_t(const void* logits, int64_t rs, int64_t n, int E, int k, float* w, int
   const int L = pow2_at_least(E);
   const int S = L < 32 ? L : 32;
   const int V = L / S;
-  const bool full = k > S;
-  const int64_t groups = (n + (32 / S) - 1) / (32 / S);
-  const int grid = warp_grid(groups);
-#define FK_LAUNCH(S_, V_, F_) \
-  router_fwd_kernel<T, S_, V_, F_><<<grid, 256, 0, st>>>(lp, rs, n, E, k, w, idx)
-  if (S < 32) {
-    switch (S) {
-      case 1: FK_LAUNCH(1, 1, false); break;
-      case 2: FK_LAUNCH(2, 1, false); break;
-      case 4: FK_LAUNCH(4, 1, false); break;
-      case 8: FK_LAUNCH(8, 1, false); break;
-      case 16: FK_LAUNCH(16, 1, false); break;
-    }
-  } else if (!full) {
+  int r = FK_OK;
+  if (k > S) {
     switch (V) {
-      case 1: FK_LAUNCH(32, 1, false); break;
-      case 2: FK_LAUNCH(32, 2, false); break;
-      case 4: FK_LAUNCH(32, 4, false); break;
-      case 8: FK_LAUNCH(32, 8, false); break;
+      case 2: r = launch_full<T, 2>(lp, rs, n, E, k, w, idx, st); break;
+      case 4: r = launch_full<T, 4>(lp, rs, n, E, k, w, idx, st); break;
+      case 8: r = launch_full<T, 8>(lp, rs, n, E, k, w, idx, st); break;
+    }
+  } else if (S < 32) {
+    switch (S) {
+      case 1: r = launch_gm<T, 1, 1>(lp, rs, n, E, k, w, idx, st); break;
+      case 2: r = launch_gm<T, 2, 1>(lp, rs, n, E, k, w, idx, st); break;
+      case 4: r = launch_gm<T, 4, 1>(lp, rs, n, E, k, w, idx, st); break;
+      case 8: r = launch_gm<T, 8, 1>(lp, rs, n, E, k, w, idx, st); break;
+      case 16: r = launch_gm<T, 16, 1>(lp, rs, n, E, k, w, idx, st); break;
     }
   } else {
     switch (V) {
-      case 2: FK_LAUNCH(32, 2, true); break;
-      case 4: FK_LAUNCH(32, 4, true); break;
-      case 8: FK_LAUNCH(32, 8, true); break;
+      case 1: r = launch_gm<T, 32, 1>(lp, rs, n, E, k, w, idx, st); break;
+      case 2: r = launch_gm<T, 32, 2>(lp, rs, n, E, k, w, idx, st); break;
+      case 4: r = launch_gm<T, 32, 4>(lp, rs, n, E, k, w, idx, st); break;
+      case 8: r = launch_gm<T, 32, 8>(lp, rs, n, E, k, w, idx, st); break;
     }
   }
-#undef FK_LAUNCH
+  if (r != FK_OK) return r;
   return launch_status("fk_router_fwd");
 }
 

@@ -35,7 +35,7 @@ def test_swiglu_matches_oracle(dtype, shape):
 
 def test_swiglu_unaligned_views():
     G = gen(4)
-    base = torch.randn(3, 1001, generator=G).cuda()
+    base = torch.randn(3, 1003, generator=G).cuda()
     gate, up = base[0, 1:1000], base[1, 3:1002]  # offsets break 16-byte alignment
     out = fk.fused_swiglu(gate, up)
     ref = swiglu_oracle(gate.cpu(), up.cpu())
