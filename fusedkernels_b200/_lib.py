@@ -33,6 +33,17 @@ SIGNATURES: dict[str, list] = {
     "fk_ce_fwd": [_vp, _i64, _vp, _i64, _vp, _i64, _i64, _i64, _f32, _i32, _vp, _vp, _vp, _vp,
                   _vp],
     "fk_ce_bwd_scale": [_vp, _i64, _i64, _i64, _vp, _i32, _vp],
+    "fk_moe_capacity": [_i64, _i32, _i32, C.POINTER(_i64), C.POINTER(_sz)],
+    "fk_moe_route_meta": [_vp, _vp, _i64, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64,
+                          _vp, _sz, _vp, _vp],
+    "fk_moe_gather": [_vp, _i32, _vp, _i32, _vp, _i64, _vp, _i32, _vp],
+    "fk_moe_combine": [_vp, _i32, _vp, _vp, _i64, _i32, _vp, _i32, _vp],
+    "fk_moe_combine_bwd": [_vp, _vp, _i32, _vp, _vp, _i32, _vp, _i64, _vp, _vp, _i32, _vp],
+    "fk_moe_gemm_up": [_vp, _i64, _i32, _vp, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp],
+    "fk_moe_gemm_down": [_vp, _i64, _i32, _vp, _i32, _i32, _vp, _vp, _vp, _vp, _vp],
+    "fk_moe_gemm_down_dgrad": [_vp, _i64, _i32, _vp, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp],
+    "fk_moe_gemm_up_dgrad": [_vp, _i64, _i32, _vp, _i32, _i32, _vp, _vp, _vp, _vp, _vp],
+    "fk_moe_gemm_wgrad": [_vp, _i32, _vp, _i32, _i64, _vp, _i32, _vp, _vp, _vp],
 }
 _RESTYPES = {"fk_status_string": C.c_char_p, "fk_last_error": C.c_char_p}
 
@@ -99,4 +110,20 @@ def rmsnorm_bwd_workspace_bytes(rows: int, cols: int, device: torch.device) -> i
             check(load().fk_rmsnorm_bwd_workspace_size(rows, cols, C.byref(out)),
                   "fk_rmsnorm_bwd_workspace_size")
         v = _ws_cache[key] = out.value
+    return v
+
+
+_cap_cache: dict = {}
+
+
+def moe_capacity(n_tokens: int, k: int, n_experts: int) -> tuple[int, int]:
+    """(max sorted rows, metadata workspace bytes) for a routing of this size."""
+    key = (n_tokens, k, n_experts)
+    v = _cap_cache.get(key)
+    if v is None:
+        rows = C.c_int64(0)
+        ws = C.c_size_t(0)
+        check(load().fk_moe_capacity(n_tokens, k, n_experts, C.byref(rows), C.byref(ws)),
+              "fk_moe_capacity")
+        v = _cap_cache[key] = (rows.value, ws.value)
     return v

@@ -20,6 +20,8 @@
 #include "common.cuh"
 #include "ptx.cuh"
 
+#include <stdlib.h>
+
 namespace fk {
 namespace {
 
@@ -372,6 +374,154 @@ __global__ void __launch_bounds__(kCeThreads) ce_cluster_kernel(
   ptx::cluster_sync();  // no CTA leaves while a peer may still read its slots
 }
 
+// Two-sweep row kernel: one CTA of 1024 threads per row (one CTA per SM, persistent).
+// Sweep 1 streams the row from HBM with an L2 evict-last policy and keeps online
+// (max, sum exp, sum x) per thread; sweep 2 re-reads the row -- it is still in L2, the
+// 148 rows in flight occupy ~37 MB -- with evict-first and writes the gradient with
+// evict-first stores, so HBM sees one read and one write per element.
+__device__ __forceinline__ uint64_t policy_evict_last() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+__device__ __forceinline__ uint64_t policy_evict_first() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+__device__ __forceinline__ uint4 ld_hint(const void* ptr, uint64_t pol) {
+  uint4 v;
+  asm volatile("ld.global.L1::no_allocate.L2::cache_hint.v4.u32 {%0, %1, %2, %3}, [%4], %5;"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(ptr), "l"(pol));
+  return v;
+}
+__device__ __forceinline__ void st_hint(void* ptr, uint4 v, uint64_t pol) {
+  asm volatile("st.global.L1::no_allocate.L2::cache_hint.v4.u32 [%0], {%1, %2, %3, %4}, %5;" ::"l"(ptr),
+               "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w), "l"(pol)
+               : "memory");
+}
+
+constexpr int kRowThreads = 1024;
+constexpr int kRowUnroll = 4;
+
+template <typename T>
+__global__ void __launch_bounds__(kRowThreads, 1) ce_row_kernel(
+    const T* __restrict__ logits, int64_t lstride, T* grad, int64_t gstride,
+    const int64_t* __restrict__ targets, int64_t n_rows, int n_cols, int64_t ignore_index,
+    float lsm, const int* __restrict__ n_valid_p, float* __restrict__ loss_rows,
+    int* __restrict__ err) {
+  constexpr int VN = 16 / sizeof(T);
+  __shared__ float wred[3][32];
+  __shared__ float stats[2];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int nvec = n_cols / VN;
+  const uint64_t keep = policy_evict_last(), drop = policy_evict_first();
+  const float inv_nv = 1.0f / (float)(*n_valid_p);
+  const float smooth = lsm / (float)n_cols;
+  const float sub = smooth * inv_nv, hsub = (1.0f - lsm) * inv_nv;
+  for (int64_t row = blockIdx.x; row < n_rows; row += gridDim.x) {
+    const T* src = logits + row * lstride;
+    const int64_t t = targets[row];
+    Online o{-INFINITY, 0.f, 0.f};
+    int v = tid;
+    for (; v + (kRowUnroll - 1) * kRowThreads < nvec; v += kRowUnroll * kRowThreads) {
+      Vec16<T> p[kRowUnroll];
+#pragma unroll
+      for (int u = 0; u < kRowUnroll; ++u) p[u].u = ld_hint(src + (int64_t)(v + u * kRowThreads) * VN, keep);
+#pragma unroll
+      for (int u = 0; u < kRowUnroll; ++u) online_add_packet<T>(o, p[u]);
+    }
+    for (; v < nvec; v += kRowThreads) {
+      Vec16<T> p;
+      p.u = ld_hint(src + (int64_t)v * VN, keep);
+      online_add_packet<T>(o, p);
+    }
+    for (int i = nvec * VN + tid; i < n_cols; i += kRowThreads) online_add_scalar<T>(o, Elt<T>::to_f(src[i]));
+    o = warp_combine<T>(o);
+    if (lane == 0) {
+      wred[0][warp] = o.m;
+      wred[1][warp] = o.s;
+      wred[2][warp] = o.sx;
+    }
+    __syncthreads();
+    if (warp == 0) {
+      Online c{wred[0][lane], wred[1][lane], wred[2][lane]};
+      c = warp_combine<T>(c);
+      if (lane == 0) {
+        const float lse = c.m + logf(c.s);
+        stats[0] = lse;
+        const bool ignored = (t == ignore_index);
+        const bool invalid = !ignored && (t < 0 || t >= n_cols);
+        float loss = invalid ? 0.f : lse - Elt<T>::to_f(src[ignored ? 0 : t]);
+        if (lsm > 0.f) loss = (1.0f - lsm) * loss + lsm * (lse - c.sx / (float)n_cols);
+        if (ignored) loss = 0.f;
+        if (invalid) {
+          loss = __int_as_float(0x7fc00000);
+          atomicExch(err, 1);
+        }
+        loss_rows[row] = loss;
+      }
+    }
+    __syncthreads();
+    const float lse = stats[0];
+    const bool ignored = (t == ignore_index);
+    const bool invalid = !ignored && (t < 0 || t >= n_cols);
+    T* dst = grad + row * gstride;
+    if (ignored || invalid) {
+      const T z = Elt<T>::from_f(invalid ? __int_as_float(0x7fc00000) : 0.f);
+      Vec16<T> zz;
+#pragma unroll
+      for (int e = 0; e < VN; ++e) zz.e[e] = z;
+      for (int w = tid; w < nvec; w += kRowThreads) st_hint(dst + (int64_t)w * VN, zz.u, drop);
+      for (int i = nvec * VN + tid; i < n_cols; i += kRowThreads) dst[i] = z;
+    } else {
+      const float cexp = lse * kLog2e - log2f(inv_nv);
+      auto gval = [&](float x) -> float {
+        if constexpr (sizeof(T) == 4) return expf(x - lse) * inv_nv - sub;
+        else return ex2f(fmaf(x, kLog2e, -cexp)) - sub;
+      };
+      const int tv = (int)(t / VN);
+      int w = tid;
+      for (; w + (kRowUnroll - 1) * kRowThreads < nvec; w += kRowUnroll * kRowThreads) {
+        Vec16<T> p[kRowUnroll];
+#pragma unroll
+        for (int u = 0; u < kRowUnroll; ++u) p[u].u = ld_hint(src + (int64_t)(w + u * kRowThreads) * VN, drop);
+#pragma unroll
+        for (int u = 0; u < kRowUnroll; ++u) {
+          const int vv = w + u * kRowThreads;
+          float g[VN];
+#pragma unroll
+          for (int e = 0; e < VN; ++e) g[e] = gval(Elt<T>::to_f(p[u].e[e]));
+          if (vv == tv && t < (int64_t)nvec * VN) g[t - (int64_t)vv * VN] -= hsub;
+          Vec16<T> o2;
+#pragma unroll
+          for (int e = 0; e < VN; ++e) o2.e[e] = Elt<T>::from_f(g[e]);
+          st_hint(dst + (int64_t)vv * VN, o2.u, drop);
+        }
+      }
+      for (; w < nvec; w += kRowThreads) {
+        Vec16<T> p;
+        p.u = ld_hint(src + (int64_t)w * VN, drop);
+        float g[VN];
+#pragma unroll
+        for (int e = 0; e < VN; ++e) g[e] = gval(Elt<T>::to_f(p.e[e]));
+        if (w == tv && t < (int64_t)nvec * VN) g[t - (int64_t)w * VN] -= hsub;
+        Vec16<T> o2;
+#pragma unroll
+        for (int e = 0; e < VN; ++e) o2.e[e] = Elt<T>::from_f(g[e]);
+        st_hint(dst + (int64_t)w * VN, o2.u, drop);
+      }
+      for (int i = nvec * VN + tid; i < n_cols; i += kRowThreads) {
+        float g = gval(Elt<T>::to_f(src[i]));
+        if ((int64_t)i == t) g -= hsub;
+        dst[i] = Elt<T>::from_f(g);
+      }
+    }
+    __syncthreads();  // in-place: every read of this row precedes the next row's stats
+  }
+}
+
 // Fallback for rows longer than the cluster path holds: one CTA per row, three sweeps.
 template <typename T>
 __global__ void __launch_bounds__(kCeThreads) ce_generic_kernel(
@@ -467,7 +617,17 @@ int fwd_t(const void* logits, int64_t ls, void* grad, int64_t gs, const int64_t*
     };
     while (C < 8 && slice(C) * (int64_t)sizeof(T) > kMaxClusterBytes) C <<= 1;
     const int64_t chunk = slice(C);
-    if (chunk * (int64_t)sizeof(T) <= kMaxSliceBytes) {
+    const int rowvec = aligned16(lp) && aligned16(gp) && ((ls * (int64_t)sizeof(T)) % 16 == 0) &&
+                       ((gs * (int64_t)sizeof(T)) % 16 == 0);
+    const char* path = getenv("FKB200_CE_PATH");
+    const bool use_row = rowvec && !(path && path[0] == 'c');
+    if (use_row) {
+      int64_t g = n_rows < (int64_t)num_sms() ? n_rows : (int64_t)num_sms();
+      ce_row_kernel<T><<<(int)g, kRowThreads, 0, st>>>(lp, ls, gp, gs, targets, n_rows, (int)n_cols,
+                                                       ignore, lsm, n_valid, loss_rows, err);
+      int s1 = launch_status("fk_ce_fwd(row)");
+      if (s1 != FK_OK) return s1;
+    } else if (chunk * (int64_t)sizeof(T) <= kMaxSliceBytes) {
       const int smem = (int)(2 * chunk * sizeof(T));
       auto kern = ce_cluster_kernel<T>;
       cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);

@@ -437,22 +437,26 @@ __global__ void rmsnorm_bwd_generic(const T* __restrict__ dy, const T* __restric
   }
 }
 
-// dw[c] = sum_{g < G} part[g][c], fixed order, then cast to W.
+// dw[c] = sum_{g < G} part[g][c] in a fixed order, then cast to W.  One CTA of 32 warps
+// per 32 columns: warp w sums partial rows w, w+32, ... (all loads in flight), the 32
+// warp sums are added in warp order.
 template <typename W>
-__global__ void rmsnorm_dw_reduce(const float* __restrict__ part, int G, int64_t cols,
-                                  W* __restrict__ dw) {
-  for (int64_t c = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; c < cols;
-       c += (int64_t)gridDim.x * blockDim.x) {
-    float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
-    int g = 0;
-    for (; g + 3 < G; g += 4) {
-      s0 += part[(int64_t)g * cols + c];
-      s1 += part[(int64_t)(g + 1) * cols + c];
-      s2 += part[(int64_t)(g + 2) * cols + c];
-      s3 += part[(int64_t)(g + 3) * cols + c];
-    }
-    for (; g < G; ++g) s0 += part[(int64_t)g * cols + c];
-    dw[c] = Elt<W>::from_f((s0 + s1) + (s2 + s3));
+__global__ void __launch_bounds__(1024) rmsnorm_dw_reduce(const float* __restrict__ part, int G,
+                                                          int64_t cols, W* __restrict__ dw) {
+  __shared__ float red[32][33];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t c = (int64_t)blockIdx.x * 32 + lane;
+  float s = 0.f;
+  if (c < cols) {
+#pragma unroll 8
+    for (int g = warp; g < G; g += 32) s += part[(int64_t)g * cols + c];
+  }
+  red[warp][lane] = s;
+  __syncthreads();
+  if (warp == 0 && c < cols) {
+    float t = 0.f;
+    for (int w = 0; w < 32; ++w) t += red[w][lane];
+    dw[c] = Elt<W>::from_f(t);
   }
 }
 
@@ -596,9 +600,8 @@ int bwd_t(const void* dy, const void* x, const void* w, const float* rstd, void*
   }
   int st = launch_status("fk_rmsnorm_bwd");
   if (st != FK_OK) return st;
-  int rgrid = (int)((cols + 255) / 256);
-  if (rgrid > num_sms() * 4) rgrid = num_sms() * 4;
-  rmsnorm_dw_reduce<W><<<rgrid, 256, 0, s>>>(part, grid, cols, static_cast<W*>(dw));
+  const int rgrid = (int)((cols + 31) / 32);
+  rmsnorm_dw_reduce<W><<<rgrid, 1024, 0, s>>>(part, grid, cols, static_cast<W*>(dw));
   return launch_status("fk_rmsnorm_bwd(dw reduce)");
 }
 

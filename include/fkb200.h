@@ -120,6 +120,79 @@ FK_API int fk_ce_fwd(const void* logits, int64_t row_stride, void* grad, int64_t
 FK_API int fk_ce_bwd_scale(void* grad, int64_t grad_row_stride, int64_t n_rows, int64_t n_cols,
                     const float* grad_output, int dtype, void* stream);
 
+/* ---------------------------------------------------------------- MoE sorted dispatch
+ * Sorted-row layout: the n_tokens*k (token, slot) assignments are laid out expert-major,
+ * each expert's segment padded to a multiple of 128 rows (padding rows hold assignment
+ * -1 and zero activations); inside a segment assignments keep (token, slot) order.
+ * Every buffer is sized by the shapes alone (max_rows), so no device->host copy is needed.
+ * Replaces the argsort / gather / bincount / cumsum / .tolist() / per-expert loop /
+ * index_add_ of moe_layer_sorted.py:50-85. */
+
+/* max_rows = round_up(n_tokens*k + n_experts*127, 128) and the metadata workspace size. */
+FK_API int fk_moe_capacity(int64_t n_tokens, int k, int n_experts, int64_t* max_rows,
+                           size_t* meta_workspace_bytes);
+
+/* From idx/w [n_tokens, k] (int64 / fp32): counts[E], seg_start[E+1] (padded row offsets),
+ * tile_expert[max_rows/128] (expert of each 128-row block, -1 past the end), n_mblk[1]
+ * (valid 128-row blocks), sorted_assign/sorted_w[max_rows] (assignment index t*k+j and its
+ * weight per sorted row), slot_pos[n_tokens*k] (sorted row of each assignment).
+ * Deterministic (stable counting sort).  An expert id outside [0, E) sets *err_flag = 1.
+ * Replaces moe_layer_sorted.py:50-68. */
+FK_API int fk_moe_route_meta(const int64_t* idx, const float* w, int64_t n_tokens, int k,
+                             int n_experts, int* counts, int* seg_start, int* tile_expert,
+                             int* n_mblk, int* sorted_assign, float* sorted_w, int* slot_pos,
+                             int64_t max_rows, void* workspace, size_t workspace_bytes,
+                             int* err_flag, void* stream);
+
+/* xs[p, :] = x[sorted_assign[p] / k, :] for the valid rows, zero for padding rows.
+ * Replaces gathered_x = x_flat[sorted_token_idx] (moe_layer_sorted.py:63). */
+FK_API int fk_moe_gather(const void* x, int dim, const int* sorted_assign, int k,
+                         const int* n_mblk, int64_t max_rows, void* xs, int dtype, void* stream);
+
+/* out[t, :] = sum_j w[t,j] * y[slot_pos[t*k+j], :] (w == NULL: plain sum), fp32
+ * accumulation in slot order (deterministic).
+ * Replaces the weight multiply and index_add_ of moe_layer_sorted.py:82-85. */
+FK_API int fk_moe_combine(const void* y, int dim, const int* slot_pos, const float* w,
+                          int64_t n_tokens, int k, void* out, int dtype, void* stream);
+
+/* Backward of fk_moe_combine: dy[p, :] = sorted_w[p] * dout[token(p), :] (zero on padding
+ * rows) and dw[a] = <dout[token(a), :], y[slot_pos[a], :]> for every assignment a.
+ * Replaces the autograd of moe_layer_sorted.py:82-85. */
+FK_API int fk_moe_combine_bwd(const void* dout, const void* y, int dim,
+                              const int* sorted_assign, const float* sorted_w, int k,
+                              const int* n_mblk, int64_t max_rows, void* dy, float* dw,
+                              int dtype, void* stream);
+
+/* Expert GEMMs on tcgen05 tensor cores (bf16 in, fp32 accumulate in TMEM, bf16 out).
+ * Weights are stacked per expert: w13 [E, 2H, D] (rows 0..H-1 = w_gate, H..2H-1 = w_up of
+ * moe_layer.py:26-27), w2 [E, D, H] (w_down, moe_layer.py:28).  D and H multiples of 64.
+ * Kernel-side faults (a wait that timed out) set *err_flag to a non-zero code.
+ * fk_moe_gemm_up:   h1 = xs @ w13[e]^T ([max_rows, 2H] = gate | up), act = silu(g) * u
+ *                   (moe_layer.py:31, first two Linears and the activation).
+ * fk_moe_gemm_down: y = act @ w2[e]^T ([max_rows, D]) (moe_layer.py:31, w_down).
+ * fk_moe_gemm_down_dgrad: dh1 = SwiGLU'(dy @ w2[e], h1) ([max_rows, 2H] = dg | du).
+ * fk_moe_gemm_up_dgrad:   dxs = dh1 @ w13[e] ([max_rows, D]).
+ * fk_moe_gemm_wgrad: dw[e] = a[seg_e]^T @ b[seg_e] for every expert e ([E, m_dim, n_dim]),
+ *                   a [max_rows, m_dim], b [max_rows, n_dim] (zero for empty experts).
+ * Together they replace the per-expert cuBLAS calls of moe_layer_sorted.py:70-77 and
+ * their autograd backward. */
+FK_API int fk_moe_gemm_up(const void* xs, int64_t max_rows, int dim, const void* w13,
+                          int hidden, int n_experts, const int* tile_expert, const int* n_mblk,
+                          void* h1, void* act, int* err_flag, void* stream);
+FK_API int fk_moe_gemm_down(const void* act, int64_t max_rows, int hidden, const void* w2,
+                            int dim, int n_experts, const int* tile_expert, const int* n_mblk,
+                            void* y, int* err_flag, void* stream);
+FK_API int fk_moe_gemm_down_dgrad(const void* dy, int64_t max_rows, int dim, const void* w2,
+                                  int hidden, int n_experts, const int* tile_expert,
+                                  const int* n_mblk, const void* h1, void* dh1, int* err_flag,
+                                  void* stream);
+FK_API int fk_moe_gemm_up_dgrad(const void* dh1, int64_t max_rows, int hidden, const void* w13,
+                                int dim, int n_experts, const int* tile_expert,
+                                const int* n_mblk, void* dxs, int* err_flag, void* stream);
+FK_API int fk_moe_gemm_wgrad(const void* a, int m_dim, const void* b, int n_dim,
+                             int64_t max_rows, const int* seg_start, int n_experts, void* dw,
+                             int* err_flag, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,0 +1,319 @@
+"""MoE sorted-dispatch kernels: routing metadata (bit-exact vs a numpy stable counting
+sort), the tcgen05 grouped GEMMs (vs plain PyTorch fp32 on the GPU), and the whole
+FusedMoEMLPSorted layer vs the CPU oracle (NaiveMoEMLP restated, fp64).
+Tolerances: GEMM outputs (bf16) atol 2e-2 + rtol 2e-2 of the fp32 reference; layer out,
+dx, dW atol = rtol = 2e-2 relative to the tensor's max magnitude, with identical routing."""
+import numpy as np
+import pytest
+import torch
+import torch.nn.functional as F
+
+import fusedkernels_b200 as fk
+from fusedkernels_b200 import _lib
+from fusedkernels_b200.moe_layer_sorted import FusedMoEMLPSorted, _Plan
+from oracle import moe_layer_oracle, route_oracle, zipf_expert_bias
+from conftest import gen
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def meta(idx, w, E):
+    n, k = idx.shape
+    plan = _Plan(n, k, E, torch.device(DEV))
+    st = torch.cuda.current_stream().cuda_stream
+    _lib.call("fk_moe_route_meta", idx.data_ptr(), w.data_ptr(), n, k, E,
+              plan.counts.data_ptr(), plan.seg_start.data_ptr(), plan.tile_expert.data_ptr(),
+              plan.n_mblk.data_ptr(), plan.sorted_assign.data_ptr(), plan.sorted_w.data_ptr(),
+              plan.slot_pos.data_ptr(), plan.max_rows, plan.ws.data_ptr(), plan.ws.numel(),
+              plan.err.data_ptr(), st)
+    return plan
+
+
+def meta_reference(idx, E):
+    """numpy stable counting sort with 128-row padded segments."""
+    idx = idx.reshape(-1)
+    counts = np.bincount(idx, minlength=E)
+    pad = (counts + 127) // 128 * 128
+    seg = np.concatenate([[0], np.cumsum(pad)])
+    order = np.argsort(idx, kind="stable")
+    sorted_assign = np.full(seg[-1], -1, dtype=np.int64)
+    slot_pos = np.zeros(idx.size, dtype=np.int64)
+    fill = seg[:-1].copy()
+    for a in order:
+        e = idx[a]
+        sorted_assign[fill[e]] = a
+        slot_pos[a] = fill[e]
+        fill[e] += 1
+    return counts, seg, sorted_assign, slot_pos
+
+
+def random_routing(n, k, E, seed, skew=0.0):
+    G = gen(seed)
+    logits = torch.randn(n, E, generator=G) + skew * torch.linspace(3, -3, E)
+    w, idx = route_oracle(logits, k)
+    return w, idx
+
+
+@pytest.mark.parametrize("n,k,E,skew", [(1000, 2, 8, 0.0), (4096, 8, 128, 2.0), (5, 2, 64, 0.0),
+                                        (32768, 8, 128, 4.0)])
+def test_route_meta_matches_stable_counting_sort(n, k, E, skew):
+    w, idx = random_routing(n, k, E, n + E, skew)
+    plan = meta(idx.to(DEV), w.to(DEV), E)
+    counts, seg, sa, sp = meta_reference(idx.numpy(), E)
+    assert plan.err[0].item() == 0
+    assert np.array_equal(plan.counts.cpu().numpy(), counts)
+    assert np.array_equal(plan.seg_start.cpu().numpy(), seg)
+    nm = plan.n_mblk.item()
+    assert nm * 128 == seg[-1]
+    assert np.array_equal(plan.sorted_assign[:seg[-1]].cpu().numpy(), sa)
+    assert np.array_equal(plan.slot_pos[:n * k].cpu().numpy(), sp)
+    te = plan.tile_expert.cpu().numpy()
+    for e in range(E):
+        assert (te[seg[e] // 128:seg[e + 1] // 128] == e).all()
+    assert (te[nm:] == -1).all()
+    sw = plan.sorted_w[:seg[-1]].cpu().numpy()
+    wf = w.reshape(-1).numpy()
+    valid = sa >= 0
+    assert np.array_equal(sw[valid], wf[sa[valid]]) and (sw[~valid] == 0).all()
+
+
+def make_problem(n, k, E, D, H, seed, skew=0.0):
+    w, idx = random_routing(n, k, E, seed, skew)
+    G = gen(seed + 1)
+    x = (torch.randn(n, D, generator=G)).bfloat16().to(DEV)
+    w13 = (torch.randn(E, 2 * H, D, generator=G) * D ** -0.5).bfloat16().to(DEV)
+    w2 = (torch.randn(E, D, H, generator=G) * H ** -0.5).bfloat16().to(DEV)
+    plan = meta(idx.to(DEV), w.to(DEV), E)
+    R = plan.max_rows
+    xs = torch.empty(R, D, dtype=torch.bfloat16, device=DEV)
+    st = torch.cuda.current_stream().cuda_stream
+    _lib.call("fk_moe_gather", x.data_ptr(), D, plan.sorted_assign.data_ptr(), k,
+              plan.n_mblk.data_ptr(), R, xs.data_ptr(), _lib.FK_BF16, st)
+    return dict(n=n, k=k, E=E, D=D, H=H, w=w.to(DEV), idx=idx.to(DEV), x=x, w13=w13, w2=w2,
+                plan=plan, xs=xs, st=st)
+
+
+def expert_of_rows(plan):
+    te = plan.tile_expert.cpu()
+    rows = plan.n_mblk.item() * 128
+    return te.repeat_interleave(128)[:rows].to(DEV), rows
+
+
+def close(got, ref, tol=2e-2):
+    got = got.float()
+    ref = ref.float()
+    scale = max(ref.abs().max().item(), 1e-6)
+    err = (got - ref).abs().max().item()
+    assert err <= tol * scale + tol * 0.1, f"max abs err {err:.4g} vs scale {scale:.4g}"
+
+
+SHAPES = [(512, 2, 8, 256, 128), (300, 4, 16, 64, 64), (2048, 4, 16, 1024, 512),
+          (64, 8, 128, 128, 256)]
+
+
+@pytest.mark.parametrize("n,k,E,D,H", SHAPES)
+def test_gather_and_gemm_up_down(n, k, E, D, H):
+    P = make_problem(n, k, E, D, H, seed=n + D)
+    plan, R = P["plan"], P["plan"].max_rows
+    xs = P["xs"]
+    eor, rows = expert_of_rows(plan)
+    sa = plan.sorted_assign[:rows].long()
+    ref_xs = torch.where((sa >= 0)[:, None], P["x"][sa.clamp(min=0) // k], 0)
+    assert torch.equal(xs[:rows], ref_xs)
+    h1 = torch.empty(R, 2 * H, dtype=torch.bfloat16, device=DEV)
+    act = torch.empty(R, H, dtype=torch.bfloat16, device=DEV)
+    y = torch.empty(R, D, dtype=torch.bfloat16, device=DEV)
+    eptr = plan.err.data_ptr() + 4
+    _lib.call("fk_moe_gemm_up", xs.data_ptr(), R, D, P["w13"].data_ptr(), H, E,
+              plan.tile_expert.data_ptr(), plan.n_mblk.data_ptr(), h1.data_ptr(), act.data_ptr(),
+              eptr, P["st"])
+    _lib.call("fk_moe_gemm_down", act.data_ptr(), R, H, P["w2"].data_ptr(), D, E,
+              plan.tile_expert.data_ptr(), plan.n_mblk.data_ptr(), y.data_ptr(), eptr, P["st"])
+    torch.cuda.synchronize()
+    assert plan.err[1].item() == 0
+    xf = xs[:rows].float()
+    ref_h1 = torch.einsum("rd,rjd->rj", xf, P["w13"].float()[eor])
+    close(h1[:rows], ref_h1)
+    g, u = ref_h1[:, :H], ref_h1[:, H:]
+    ref_act = F.silu(g) * u
+    close(act[:rows], ref_act)
+    ref_y = torch.einsum("rh,rdh->rd", act[:rows].float(), P["w2"].float()[eor])
+    close(y[:rows], ref_y)
+
+
+@pytest.mark.parametrize("n,k,E,D,H", SHAPES)
+def test_gemm_backward_pieces(n, k, E, D, H):
+    P = make_problem(n, k, E, D, H, seed=2 * n + D)
+    plan, R = P["plan"], P["plan"].max_rows
+    eor, rows = expert_of_rows(plan)
+    G = gen(99)
+    sa = plan.sorted_assign[:rows]
+    valid = (sa >= 0)[:, None]
+    dy = torch.where(valid, torch.randn(rows, D, generator=G).bfloat16().to(DEV), 0)
+    h1 = torch.where(valid, torch.randn(rows, 2 * H, generator=G).bfloat16().to(DEV), 0)
+    dyb = torch.zeros(R, D, dtype=torch.bfloat16, device=DEV)
+    dyb[:rows] = dy
+    h1b = torch.zeros(R, 2 * H, dtype=torch.bfloat16, device=DEV)
+    h1b[:rows] = h1
+    dh1 = torch.empty(R, 2 * H, dtype=torch.bfloat16, device=DEV)
+    dxs = torch.empty(R, D, dtype=torch.bfloat16, device=DEV)
+    dw2 = torch.empty(E, D, H, dtype=torch.bfloat16, device=DEV)
+    dw13 = torch.empty(E, 2 * H, D, dtype=torch.bfloat16, device=DEV)
+    act = torch.where(valid, torch.randn(rows, H, generator=G).bfloat16().to(DEV), 0)
+    actb = torch.zeros(R, H, dtype=torch.bfloat16, device=DEV)
+    actb[:rows] = act
+    eptr = plan.err.data_ptr() + 4
+    st = P["st"]
+    _lib.call("fk_moe_gemm_down_dgrad", dyb.data_ptr(), R, D, P["w2"].data_ptr(), H, E,
+              plan.tile_expert.data_ptr(), plan.n_mblk.data_ptr(), h1b.data_ptr(), dh1.data_ptr(),
+              eptr, st)
+    _lib.call("fk_moe_gemm_up_dgrad", dh1.data_ptr(), R, H, P["w13"].data_ptr(), D, E,
+              plan.tile_expert.data_ptr(), plan.n_mblk.data_ptr(), dxs.data_ptr(), eptr, st)
+    _lib.call("fk_moe_gemm_wgrad", dyb.data_ptr(), D, actb.data_ptr(), H, R,
+              plan.seg_start.data_ptr(), E, dw2.data_ptr(), eptr, st)
+    _lib.call("fk_moe_gemm_wgrad", dh1.data_ptr(), 2 * H, P["xs"].data_ptr(), D, R,
+              plan.seg_start.data_ptr(), E, dw13.data_ptr(), eptr, st)
+    torch.cuda.synchronize()
+    assert plan.err[1].item() == 0
+    dact = torch.einsum("rd,rdh->rh", dy.float(), P["w2"].float()[eor])
+    g, u = h1[:, :H].float(), h1[:, H:].float()
+    s = torch.sigmoid(g)
+    ref_dh1 = torch.cat([dact * u * s * (1 + g * (1 - s)), dact * g * s], dim=1)
+    close(dh1[:rows], ref_dh1)
+    ref_dxs = torch.einsum("rj,rjd->rd", dh1[:rows].float(), P["w13"].float()[eor])
+    close(dxs[:rows], ref_dxs)
+    seg = plan.seg_start.cpu().tolist()
+    for e in range(E):
+        a, b = seg[e], seg[e + 1]
+        ref2 = dy[a:b].float().t() @ act[a:b].float()
+        ref13 = dh1[a:b].float().t() @ P["xs"][a:b].float()
+        if b == a:
+            assert torch.count_nonzero(dw2[e]) == 0 and torch.count_nonzero(dw13[e]) == 0
+        else:
+            close(dw2[e], ref2)
+            close(dw13[e], ref13)
+
+
+def run_layer(layer, x, dout, bias=None):
+    logits_box = {}
+
+    def hook(mod, inp, out):
+        if bias is not None:
+            out = out + bias.to(out.dtype)
+        logits_box["l"] = out.detach()
+        return out
+
+    h = layer.router.register_forward_hook(hook)
+    xg = x.clone().requires_grad_(True)
+    out = layer(xg)
+    out.backward(dout)
+    h.remove()
+    return out.detach(), xg.grad, logits_box["l"]
+
+
+def stacked_grads(layer):
+    E = layer.n_experts
+    g13 = torch.stack([torch.cat([ex.w_gate.weight.grad, ex.w_up.weight.grad]) for ex in layer.experts])
+    g2 = torch.stack([ex.w_down.weight.grad for ex in layer.experts])
+    return g13, g2
+
+
+@pytest.mark.parametrize("E,k", [(8, 2), (32, 4), (64, 8), (128, 16)])
+def test_layer_matches_oracle(E, k):
+    """tests/test_moe_sorted_dispatch.py:43-69 shapes (B=2, T=128, D=256, H=512), bf16."""
+    torch.manual_seed(0)
+    D, H = 256, 512
+    layer = FusedMoEMLPSorted(D, H, E, k).to(DEV).bfloat16()
+    G = gen(E)
+    x = torch.randn(2, 128, D, generator=G).bfloat16().to(DEV)
+    dout = torch.randn(2, 128, D, generator=G).bfloat16().to(DEV)
+    out, dx, logits = run_layer(layer, x, dout)
+    H_ = H
+    w13 = layer.w13.float().cpu()
+    ro, rdx, rdwg, rdwu, rdwd, rdl = moe_layer_oracle(
+        x.reshape(-1, D).cpu(), logits.cpu(), w13[:, :H_], w13[:, H_:], layer.w2.float().cpu(), k,
+        dout.reshape(-1, D).cpu())
+    close(out.reshape(-1, D).cpu(), ro)
+    # dx: expert path + router path (logits = x @ Wr^T)
+    rdx_total = rdx + rdl @ layer.router.weight.double().cpu()
+    close(dx.reshape(-1, D).cpu(), rdx_total)
+    g13, g2 = stacked_grads(layer)
+    close(g13.cpu(), torch.cat([rdwg, rdwu], dim=1))
+    close(g2.cpu(), rdwd)
+    rdwr = rdl.t() @ x.reshape(-1, D).double().cpu()
+    close(layer.router.weight.grad.cpu(), rdwr)
+
+
+def test_layer_handles_empty_experts():
+    """tests/test_moe_sorted_dispatch.py:72-82: 4 tokens, 64 experts."""
+    torch.manual_seed(1)
+    layer = FusedMoEMLPSorted(64, 128, 64, 2).to(DEV).bfloat16()
+    x = torch.randn(1, 4, 64, device=DEV).bfloat16().requires_grad_(True)
+    out = layer(x)
+    assert out.shape == x.shape
+    out.float().sum().backward()
+    assert x.grad is not None
+    g13, g2 = stacked_grads(layer)
+    used = set()
+    with torch.no_grad():
+        _, idx = route_oracle(layer.router(x.detach().reshape(-1, 64)).float().cpu(), 2)
+    used = set(idx.reshape(-1).tolist())
+    for e in range(64):
+        if e not in used:
+            assert torch.count_nonzero(g13[e]) == 0 and torch.count_nonzero(g2[e]) == 0
+
+
+def test_layer_deterministic():
+    torch.manual_seed(2)
+    layer = FusedMoEMLPSorted(256, 256, 32, 4).to(DEV).bfloat16()
+    x = torch.randn(1024, 256, device=DEV).bfloat16()
+    dout = torch.randn(1024, 256, device=DEV).bfloat16()
+    res = []
+    for _ in range(3):
+        layer.zero_grad(set_to_none=True)
+        out, dx, _ = run_layer(layer, x, dout)
+        g13, g2 = stacked_grads(layer)
+        res.append((out, dx, g13, g2, layer.router.weight.grad.clone()))
+    for r in res[1:]:
+        assert all(torch.equal(a, b) for a, b in zip(r, res[0]))
+
+
+def test_layer_state_dict_keys_and_error_flags():
+    layer = FusedMoEMLPSorted(128, 128, 8, 2).to(DEV).bfloat16()
+    keys = list(layer.state_dict().keys())
+    assert keys[0] == "router.weight" and "experts.7.w_down.weight" in keys and len(keys) == 25
+    layer.check_errors = True
+    x = torch.randn(64, 128, device=DEV).bfloat16().requires_grad_(True)
+    layer(x).float().sum().backward()
+
+
+def test_layer_workload_shape_sampled_tokens():
+    """x [32768, 4096] bf16, E=128, k=8, H=1024, Zipf(1.1) expert bias on the logits:
+    16 sampled tokens' outputs and input gradients vs a per-token fp64 evaluation."""
+    torch.manual_seed(3)
+    N, D, H, E, k = 32768, 4096, 1024, 128, 8
+    layer = FusedMoEMLPSorted(D, H, E, k)
+    with torch.no_grad():
+        layer.router.weight.normal_(0, 0.02)
+        for ex in layer.experts:
+            for lin in (ex.w_gate, ex.w_up, ex.w_down):
+                lin.weight.normal_(0, 0.02)
+    layer = layer.to(DEV).bfloat16()
+    G = gen(4)
+    x = torch.randn(N, D, generator=G).bfloat16().to(DEV)
+    dout = torch.randn(N, D, generator=G).bfloat16().to(DEV)
+    bias = zipf_expert_bias(E).to(DEV)
+    out, dx, logits = run_layer(layer, x, dout, bias=bias)
+    toks = torch.randint(0, N, (16,), generator=G)
+    w, idx = route_oracle(logits.float().cpu()[toks], k)
+    for i, t in enumerate(toks.tolist()):
+        xt = x[t].double()
+        ref = torch.zeros(D, dtype=torch.float64, device=DEV)
+        for j in range(k):
+            e = idx[i, j].item()
+            h = layer.w13[e].double() @ xt
+            a = F.silu(h[:H]) * h[H:]
+            ref += w[i, j].item() * (layer.w2[e].double() @ a)
+        close(out[t], ref)
+    assert torch.isfinite(dx).all()
