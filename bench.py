@@ -143,6 +143,7 @@ def make_graph(fn, inner):
 # ----------------------------------------------------------------------------- workloads --
 class Workload:
     graph_inner = 1
+    use_graph = True
     name = ""
     metric = ""
     unit = ""
@@ -494,7 +495,147 @@ class Router(Workload):
                       "inputs 33 MB: HBM/L2 streaming"}
 
 
-WORKLOADS = {"rmsnorm": RMSNorm, "swiglu": SwiGLU, "ce": CrossEntropy, "router": Router}
+class MoELayer(Workload):
+    """Sorted-dispatch MoE layer fwd+bwd: x [32768, 4096] bf16 ~N(0,1); router
+    Linear(4096 -> 128) weights ~N(0, 0.02) plus a per-expert logit bias 2*ln(w_e),
+    w_e ~ (e+1)^-1.1 normalised (added to the router output by a forward hook, as the
+    workload specifies); k = 8; experts SwiGLU with hidden 1024, weights ~N(0, 0.02) bf16;
+    upstream gradient ~N(0,1).  Algorithmic FLOPs: 6 GEMM passes over the 262144 real
+    (token, expert) assignments (2*M*K*N each) plus the router GEMM fwd+bwd."""
+    name = "moe"
+    metric = "MoE layer fwd+bwd throughput"
+    unit = "tokens/s"
+    tokens, dim, hidden, E, k = 32768, 4096, 1024, 128, 8
+    use_graph = False
+
+    def setup(self, dev):
+        import fusedkernels_b200 as fk
+        from fusedkernels_b200 import _lib
+        from oracle import zipf_expert_bias
+        self.lib = _lib
+        torch.manual_seed(0)
+        layer = fk.FusedMoEMLPSorted(self.dim, self.hidden, self.E, self.k)
+        with torch.no_grad():
+            layer.router.weight.normal_(0, 0.02)
+            for ex in layer.experts:
+                for lin in (ex.w_gate, ex.w_up, ex.w_down):
+                    lin.weight.normal_(0, 0.02)
+        self.layer = layer.to(dev).bfloat16()
+        bias = zipf_expert_bias(self.E).to(dev).bfloat16()
+        self.layer.router.register_forward_hook(lambda m, i, o: o + bias)
+        G = gen(0)
+        self.x_h = torch.randn(self.tokens, self.dim, generator=G).bfloat16().pin_memory()
+        self.d_h = torch.randn(self.tokens, self.dim, generator=G).bfloat16().pin_memory()
+        self.x = self.x_h.to(dev)
+        self.dout = self.d_h.to(dev)
+        self.dev = dev
+        A = self.tokens * self.k
+        D, H = self.dim, self.hidden
+        self.flops = 3 * (2 * A * 2 * H * D + 2 * A * D * H) + 3 * 2 * self.tokens * D * self.E
+        self.up_flops = 2 * A * 2 * H * D
+        # one routing for the kernel-level timing of the up-projection GEMM
+        self._prep_kernel()
+
+    def _prep_kernel(self):
+        from fusedkernels_b200.moe_layer_sorted import _Plan
+        with torch.no_grad():
+            logits = self.layer.router(self.x)
+            import fusedkernels_b200 as fk
+            w, idx = fk.fused_moe_route_v2(logits, self.k)
+        plan = _Plan(self.tokens, self.k, self.E, self.dev)
+        st = cur_stream()
+        L = self.lib
+        L.call("fk_moe_route_meta", idx.data_ptr(), w.data_ptr(), self.tokens, self.k, self.E,
+               plan.counts.data_ptr(), plan.seg_start.data_ptr(), plan.tile_expert.data_ptr(),
+               plan.n_mblk.data_ptr(), plan.sorted_assign.data_ptr(), plan.sorted_w.data_ptr(),
+               plan.slot_pos.data_ptr(), plan.max_rows, plan.ws.data_ptr(), plan.ws.numel(),
+               plan.err.data_ptr(), st)
+        R = plan.max_rows
+        bf = dict(dtype=torch.bfloat16, device=self.dev)
+        self.kp = plan
+        self.kxs = torch.empty(R, self.dim, **bf)
+        L.call("fk_moe_gather", self.x.data_ptr(), self.dim, plan.sorted_assign.data_ptr(), self.k,
+               plan.n_mblk.data_ptr(), R, self.kxs.data_ptr(), L.FK_BF16, st)
+        self.kh1 = torch.empty(R, 2 * self.hidden, **bf)
+        self.kact = torch.empty(R, self.hidden, **bf)
+        self.ky = torch.empty(R, self.dim, **bf)
+
+    def gemm_up(self):
+        p = self.kp
+        self.lib.call("fk_moe_gemm_up", self.kxs.data_ptr(), p.max_rows, self.dim,
+                      self.layer.w13.data_ptr(), self.hidden, self.E, p.tile_expert.data_ptr(),
+                      p.n_mblk.data_ptr(), self.kh1.data_ptr(), self.kact.data_ptr(),
+                      p.err.data_ptr() + 4, cur_stream())
+
+    def gemm_down(self):
+        p = self.kp
+        self.lib.call("fk_moe_gemm_down", self.kact.data_ptr(), p.max_rows, self.hidden,
+                      self.layer.w2.data_ptr(), self.dim, self.E, p.tile_expert.data_ptr(),
+                      p.n_mblk.data_ptr(), self.ky.data_ptr(), p.err.data_ptr() + 4, cur_stream())
+
+    def step(self):
+        self.layer.zero_grad(set_to_none=True)
+        x = self.x.requires_grad_(False).detach().requires_grad_(True)
+        out = self.layer(x)
+        out.backward(self.dout)
+
+    launches_per_step = 17  # meta(2) gather up down combine | combine_bwd 2 dgrad 2 wgrad combine, router fwd/bwd
+
+    def units_per_step(self):
+        return self.tokens
+
+    def kernels(self):
+        A = self.tokens * self.k
+        return [("moe_gemm_up", self.gemm_up, self.up_flops),
+                ("moe_gemm_down", self.gemm_down, 2 * A * self.dim * self.hidden)]
+
+    def e2e_setup(self):
+        pass
+
+    def e2e_step(self):
+        self.layer.zero_grad(set_to_none=True)
+        x = self.x_h.to(self.dev, non_blocking=True).requires_grad_(True)
+        d = self.d_h.to(self.dev, non_blocking=True)
+        out = self.layer(x)
+        out.backward(d)
+        return self.layer.router.weight.grad.to("cpu", non_blocking=True)
+
+    def e2e_bytes(self):
+        return self.tokens * self.dim * 2 * 2, self.E * self.dim * 2
+
+    def cpu_sample(self):
+        return moe_cpu_sample(self, 256)
+
+    def config(self):
+        return {"workload": "moe_sorted_dispatch_fwd_bwd", "tokens": self.tokens, "dim": self.dim,
+                "hidden": self.hidden, "n_experts": self.E, "k": self.k, "dtype": "bf16",
+                "router_bias": "2*ln(zipf(1.1) rank weights)", "parallelism": "single GPU",
+                "l2": "inputs exceed L2 (x 268 MB, expert weights 3.2 GB)"}
+
+
+def moe_cpu_sample(wl, n_tok):
+    """Oracle (NaiveMoEMLP restated, fp32 on the host) on n_tok tokens of the workload with
+    full-size weight shapes (one random matrix per role shared by all experts: the values
+    do not change the work); returns (seconds, tokens, description)."""
+    from oracle import moe_layer_oracle, zipf_expert_bias
+    G = gen(1)
+    D, H, E, k = wl.dim, wl.hidden, wl.E, wl.k
+    if not hasattr(wl, "_cpu_w"):
+        wl._cpu_w = (torch.randn(E, D, generator=G) * 0.02,
+                     (torch.randn(2 * H, D, generator=G) * 0.02).expand(E, 2 * H, D),
+                     (torch.randn(D, H, generator=G) * 0.02).expand(E, D, H))
+    wr, w13, w2 = wl._cpu_w
+    x = torch.randn(n_tok, D, generator=G)
+    dout = torch.randn(n_tok, D, generator=G)
+    t0 = time.perf_counter()
+    logits = x @ wr.t() + zipf_expert_bias(E)
+    moe_layer_oracle(x, logits, w13[:, :H], w13[:, H:], w2, k, dout, dtype=torch.float32)
+    dt = time.perf_counter() - t0
+    return dt, n_tok, f"{n_tok} of {wl.tokens} tokens, full dims, fp32 NaiveMoEMLP fwd+bwd"
+
+
+WORKLOADS = {"rmsnorm": RMSNorm, "swiglu": SwiGLU, "ce": CrossEntropy, "router": Router,
+             "moe": MoELayer}
 
 
 # ----------------------------------------------------------------------------- timing --
@@ -542,19 +683,24 @@ def run_ours(args):
     # The timed steps replay a CUDA graph of the step's C-ABI launches (`inner` steps per
     # graph for launch-latency-bound workloads), so the number is device time.
     inner = wl.graph_inner
-    graph = make_graph(wl.step, inner)
+    if wl.use_graph:
+        graph = make_graph(wl.step, inner)
+        run_step = graph.replay
+    else:
+        inner = 1
+        run_step = wl.step
     reps = max(1, args.steps // inner) if inner > 1 else args.steps
     for _ in range(args.warmup):
-        graph.replay()
+        run_step()
     torch.cuda.synchronize(dev)
     barrier()
     with ClockSampler(dev.index) as clk:
         t0 = time.perf_counter()
-        ms = time_device(graph.replay, reps, stream)
+        ms = time_device(run_step, reps, stream)
         # keep the GPU loaded for ~1 s so the clock record has samples under load
         extra = 0
         while time.perf_counter() - t0 < 1.0 and extra < 20000:
-            graph.replay()
+            run_step()
             extra += 1
         torch.cuda.synchronize(dev)
     barrier()
@@ -575,9 +721,18 @@ def run_ours(args):
         kern.append({"kernel": name, "ms": round(kms, 5), "bytes": nbytes,
                      "gbs": round(nbytes / (kms / 1e3) / 1e9, 1)})
     dom = max(kern, key=lambda k: k["ms"] if wl.name != "router" else k["bytes"])
-    roof = {"bound": "hbm", "achieved": dom["gbs"], "peak": pk["hbm_gbs"], "unit": "GB/s",
-            "frac": round(dom["gbs"] / pk["hbm_gbs"], 4), "traffic": ncu_traffic(dom["kernel"]),
-            "kernel": dom["kernel"], "peak_source": pk["source"]}
+    if wl.name == "moe":
+        for kk in kern:
+            kk["tflops"] = round(kk.pop("gbs") / 1e3, 1)  # bytes field holds FLOPs here
+            kk["flops"] = kk.pop("bytes")
+        roof = {"bound": "tensor", "achieved": dom["tflops"], "peak": pk["bf16_tflops"],
+                "unit": "TFLOP/s", "frac": round(dom["tflops"] / pk["bf16_tflops"], 4),
+                "traffic": ncu_traffic(dom["kernel"]), "kernel": dom["kernel"],
+                "peak_source": pk["source"] + " (burst: kernel timed alone)"}
+    else:
+        roof = {"bound": "hbm", "achieved": dom["gbs"], "peak": pk["hbm_gbs"], "unit": "GB/s",
+                "frac": round(dom["gbs"] / pk["hbm_gbs"], 4), "traffic": ncu_traffic(dom["kernel"]),
+                "kernel": dom["kernel"], "peak_source": pk["source"]}
 
     # End to end through the public API with host buffers.
     wl.e2e_setup()
@@ -606,7 +761,10 @@ def run_ours(args):
                "dtype": wl.dtype, "data": "synthetic (seeded torch.randn, shapes of the workload)",
                "config": wl.config(), "roofline": roof, "kernels": kern, "cpu_baseline": cpu,
                "e2e": e2e, "gpu_launches": wl.launches_per_step * n_steps,
-               "timing": f"CUDA graph of {inner} step(s) replayed {reps}x, CUDA events",
+               "step_tflops": (round(wl.flops / (ms_per_step / 1e3) / 1e12, 1)
+                               if hasattr(wl, "flops") else None),
+               "timing": (f"CUDA graph of {inner} step(s) replayed {reps}x, CUDA events" if wl.use_graph
+                          else f"{reps} eager steps through the public API, CUDA events"),
                "clocks": clk.summary()}
         print(json.dumps(out), flush=True)
     if torch.distributed.is_initialized():
@@ -678,6 +836,9 @@ def wl_setup_host(wl):
             cross_entropy_oracle(x, t, dtype=torch.float32)
             return time.perf_counter() - t0, (R * C * 2 * 2 + R * 8) / 1e9, \
                 f"{R} of {wl.rows} rows x {C} per step, fp32 cross-entropy fwd+bwd"
+    elif isinstance(wl, MoELayer):
+        def once():
+            return moe_cpu_sample(wl, 128)
     elif isinstance(wl, Router):
         lg = torch.randn(wl.rows, wl.E, generator=G)
         dw = torch.randn(wl.rows, wl.k, generator=G)

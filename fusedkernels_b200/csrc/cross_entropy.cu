@@ -1,22 +1,19 @@
 // Fused cross-entropy forward + gradient, reference cross_entropy.py:24-116.
 //
 // HBM traffic is one read of the logits and one write of the gradient.  A row of V
-// logits (250.5 KiB for V=128256 bf16) is larger than one SM's shared memory, so a
-// thread-block CLUSTER of C CTAs (C <= 8) owns a row: CTA c bulk-copies (cp.async.bulk,
-// mbarrier-completed) its 1/C slice of the row into shared memory, reduces it in ONE pass
-// to (max, sum exp, sum x) with an online rescale, and the C partials (plus the target
-// logit) are exchanged through distributed shared memory.  Every CTA combines the
-// partials in rank order (so all CTAs hold bit-identical statistics), then writes the
-// gradient of its slice straight from shared memory.  Nothing is re-read from HBM.
-// Clusters are persistent and walk rows r = cluster_id, += n_clusters; each CTA holds two
-// slice buffers and copies row r+1 while it works on row r; partial slots are
-// double-buffered by row parity so one cluster barrier per row suffices.  Exponentials
-// of 16-bit inputs are single ex2 instructions with log2(e) folded into an FMA.
+// logits (250.5 KiB for V=128256 bf16) is larger than one SM's shared memory; instead of
+// splitting it across CTAs, one persistent CTA of 1024 threads per SM owns a row and
+// sweeps it twice: the first sweep reduces it to (max, sum exp, sum x) with an online
+// rescale, the second writes the gradient.  Both sweeps read from L2: the row is brought
+// in by an asynchronous bulk prefetch (cp.async.bulk.prefetch.L2, evict-last policy)
+// issued one row ahead, so the HBM read is the prefetch alone and overlaps the sweeps
+// of earlier rows.  Exponentials of 16-bit inputs are single ex2 instructions with
+// log2(e) folded into an FMA.
 //
 // The mean-reduction scale 1/n_valid is folded into the gradient write (n_valid comes
 // from a one-CTA prologue that counts non-ignored targets), and the scalar loss is a
-// fixed-order reduction of the per-row losses (deterministic).  Rows longer than
-// 8 x 108 KiB fall back to a three-sweep kernel that re-reads the row from global memory.
+// fixed-order reduction of the per-row losses (deterministic).  Rows that are not
+// 16-byte aligned use a scalar three-sweep kernel.
 #include "common.cuh"
 #include "ptx.cuh"
 
@@ -26,9 +23,6 @@ namespace fk {
 namespace {
 
 constexpr int kCeThreads = 256;
-constexpr int kMaxClusterBytes = 32 * 1024;   // target slice size per CTA
-constexpr int kMaxSliceBytes = 108 * 1024;    // hard cap: two slices in shared memory
-constexpr uint32_t kBulkPiece = 32 * 1024;    // bytes per cp.async.bulk instruction
 
 template <typename T>
 __device__ __forceinline__ float fexp(float x) { return __expf(x); }
@@ -183,202 +177,12 @@ __device__ __forceinline__ Online warp_combine(Online o) {
   return o;
 }
 
-template <typename T>
-__global__ void __launch_bounds__(kCeThreads) ce_cluster_kernel(
-    const T* __restrict__ logits, int64_t lstride, T* grad, int64_t gstride,
-    const int64_t* __restrict__ targets, int64_t n_rows, int n_cols, int64_t ignore_index,
-    float lsm, const int* __restrict__ n_valid_p, float* __restrict__ loss_rows,
-    int* __restrict__ err, int chunk, int bulk, int gvec) {
-  constexpr int VN = 16 / sizeof(T);
-  extern __shared__ __align__(128) unsigned char smem_raw[];
-  auto buf_of = [&](int b) { return reinterpret_cast<T*>(smem_raw + (size_t)b * chunk * sizeof(T)); };
-  __shared__ __align__(8) uint64_t full[2];
-  __shared__ float slots[2][4];  // [row parity] {max, sum exp, sum x, target logit}
-  __shared__ float wred[3][8];
-  __shared__ float stats[4];     // combined {lse, sum x, target logit}
-  __shared__ int dead;
-
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const uint32_t crank = ptx::cluster_ctarank();
-  const uint32_t csize = ptx::cluster_nctarank();
-  const int64_t c0 = (int64_t)crank * chunk;
-  int my_len = (int)((int64_t)n_cols - c0);
-  if (my_len > chunk) my_len = chunk;
-  if (my_len < 0) my_len = 0;
-  const int bulk_len = bulk ? (my_len / VN) * VN : 0;
-  const uint32_t bulk_bytes = (uint32_t)bulk_len * sizeof(T);
-  const int nvec = my_len / VN;
-
-  const int64_t row0 = ptx::cluster_id_x();
-  const int64_t rstep = ptx::nclusters_x();
-  auto issue = [&](int64_t row, int b) {
-    const unsigned char* src =
-        reinterpret_cast<const unsigned char*>(logits + row * lstride + c0);
-    unsigned char* dst = reinterpret_cast<unsigned char*>(buf_of(b));
-    ptx::fence_proxy_async_smem();
-    ptx::mbar_arrive_expect_tx(&full[b], bulk_bytes);
-    for (uint32_t off = 0; off < bulk_bytes; off += kBulkPiece) {
-      uint32_t n = bulk_bytes - off < kBulkPiece ? bulk_bytes - off : kBulkPiece;
-      ptx::bulk_g2s(dst + off, src + off, n, &full[b]);
-    }
-  };
-
-  if (tid == 0) {
-    ptx::mbar_init(&full[0], 1);
-    ptx::mbar_init(&full[1], 1);
-    ptx::fence_mbar_init();
-    dead = 0;
-  }
-  __syncthreads();
-  if (tid == 0 && bulk_len > 0 && row0 < n_rows) issue(row0, 0);
-
-  const float inv_nv = 1.0f / (float)(*n_valid_p);
-  const float smooth = lsm / (float)n_cols;
-  const float hit = 1.0f - lsm;
-  int it = 0;
-  for (int64_t row = row0; row < n_rows; row += rstep, ++it) {
-    const int b = it & 1;
-    const int par = it & 1;
-    T* buf = buf_of(b);
-    const T* src = logits + row * lstride + c0;
-    bool poisoned = false;
-    if (bulk_len > 0) {
-      if (dead || !ptx::mbar_wait(&full[b], (uint32_t)((it >> 1) & 1))) {
-        poisoned = true;
-        if (!dead) atomicExch(err, 2);
-      }
-    }
-    for (int i = bulk_len + tid; i < my_len; i += kCeThreads) buf[i] = src[i];
-    const int64_t t = targets[row];
-    __syncthreads();
-    if (poisoned && tid == 0) dead = 1;
-    // Prefetch the next row into the other buffer (freed at the end of the last row).
-    if (tid == 0 && bulk_len > 0 && !dead && row + rstep < n_rows) issue(row + rstep, b ^ 1);
-
-    // One pass over the slice: online max / sum exp / sum x.
-    Online o{-INFINITY, 0.f, 0.f};
-    const uint4* bv = reinterpret_cast<const uint4*>(buf);
-    for (int v = tid; v < nvec; v += kCeThreads) {
-      Vec16<T> p;
-      p.u = bv[v];
-      online_add_packet<T>(o, p);
-    }
-    for (int i = nvec * VN + tid; i < my_len; i += kCeThreads)
-      online_add_scalar<T>(o, Elt<T>::to_f(buf[i]));
-    o = warp_combine<T>(o);
-    if (lane == 0) {
-      wred[0][warp] = o.m;
-      wred[1][warp] = o.s;
-      wred[2][warp] = o.sx;
-    }
-    __syncthreads();
-    if (tid == 0) {
-      Online c{wred[0][0], wred[1][0], wred[2][0]};
-      for (int w = 1; w < kCeThreads / 32; ++w) c = combine<T>(c, Online{wred[0][w], wred[1][w], wred[2][w]});
-      float xt = 0.f;
-      if (t >= c0 && t < c0 + my_len) xt = Elt<T>::to_f(buf[t - c0]);
-      slots[par][0] = c.m;
-      slots[par][1] = c.s;
-      slots[par][2] = c.sx;
-      slots[par][3] = xt;
-    }
-    ptx::cluster_sync();
-    if (tid < 32) {
-      // Lane i fetches CTA i's partials; lane 0 combines them in rank order.
-      float pm = -INFINITY, ps = 0.f, px = 0.f, pt = 0.f;
-      if ((uint32_t)tid < csize) {
-        uint32_t a = ptx::mapa(ptx::smem_u32(&slots[par][0]), (uint32_t)tid);
-        pm = ptx::ld_dsmem_f32(a);
-        ps = ptx::ld_dsmem_f32(a + 4);
-        px = ptx::ld_dsmem_f32(a + 8);
-        pt = ptx::ld_dsmem_f32(a + 12);
-      }
-      Online c{-INFINITY, 0.f, 0.f};
-      float XT = 0.f;
-      for (uint32_t i = 0; i < csize; ++i) {
-        Online q{__shfl_sync(0xffffffffu, pm, i), __shfl_sync(0xffffffffu, ps, i),
-                 __shfl_sync(0xffffffffu, px, i)};
-        c = combine<T>(c, q);
-        XT += __shfl_sync(0xffffffffu, pt, i);
-      }
-      if (tid == 0) {
-        stats[0] = c.m + logf(c.s);
-        stats[1] = c.sx;
-        stats[2] = XT;
-      }
-    }
-    __syncthreads();
-    const float lse = stats[0];
-    const bool ignored = (t == ignore_index);
-    const bool invalid = !ignored && (t < 0 || t >= n_cols);
-    if (crank == 0 && tid == 0) {
-      float loss = lse - stats[2];
-      if (lsm > 0.f) loss = (1.0f - lsm) * loss + lsm * (lse - stats[1] / (float)n_cols);
-      if (ignored) loss = 0.f;
-      if (invalid || poisoned) loss = __int_as_float(0x7fc00000);
-      loss_rows[row] = loss;
-      if (invalid) atomicExch(err, 1);
-    }
-
-    // Gradient of this slice, straight from shared memory.
-    T* dst = grad + row * gstride + c0;
-    if (ignored || invalid || poisoned) {
-      const T z = Elt<T>::from_f((invalid || poisoned) ? __int_as_float(0x7fc00000) : 0.f);
-      if (gvec) {
-        Vec16<T> zz;
-#pragma unroll
-        for (int e = 0; e < VN; ++e) zz.e[e] = z;
-        for (int v = tid; v < nvec; v += kCeThreads) st_stream(dst + v * VN, zz);
-        for (int i = nvec * VN + tid; i < my_len; i += kCeThreads) dst[i] = z;
-      } else {
-        for (int i = tid; i < my_len; i += kCeThreads) dst[i] = z;
-      }
-    } else {
-      const int64_t tl = t - c0;  // target position inside this slice (may be outside)
-      const float sub = smooth * inv_nv;
-      const float hsub = hit * inv_nv;
-      // exp(x - lse) * inv_nv == 2^(x*log2e - (lse*log2e - log2(inv_nv)))
-      const float cexp = lse * kLog2e - log2f(inv_nv);
-      auto gval = [&](float x) -> float {
-        if constexpr (sizeof(T) == 4) return expf(x - lse) * inv_nv - sub;
-        else return ex2f(fmaf(x, kLog2e, -cexp)) - sub;
-      };
-      if (gvec) {
-        const int tv = (tl >= 0 && tl < nvec * VN) ? (int)(tl / VN) : -1;
-        for (int v = tid; v < nvec; v += kCeThreads) {
-          Vec16<T> p, o;
-          p.u = bv[v];
-          float g[VN];
-#pragma unroll
-          for (int e = 0; e < VN; ++e) g[e] = gval(Elt<T>::to_f(p.e[e]));
-          if (v == tv) g[tl - (int64_t)v * VN] -= hsub;
-#pragma unroll
-          for (int e = 0; e < VN; ++e) o.e[e] = Elt<T>::from_f(g[e]);
-          st_stream(dst + v * VN, o);
-        }
-        for (int i = nvec * VN + tid; i < my_len; i += kCeThreads) {
-          float g = gval(Elt<T>::to_f(buf[i]));
-          if ((int64_t)i == tl) g -= hsub;
-          dst[i] = Elt<T>::from_f(g);
-        }
-      } else {
-        for (int i = tid; i < my_len; i += kCeThreads) {
-          float g = gval(Elt<T>::to_f(buf[i]));
-          if ((int64_t)i == tl) g -= hsub;
-          dst[i] = Elt<T>::from_f(g);
-        }
-      }
-    }
-    __syncthreads();  // this buffer is free for the copy issued two rows from now
-  }
-  ptx::cluster_sync();  // no CTA leaves while a peer may still read its slots
-}
-
 // Two-sweep row kernel: one CTA of 1024 threads per row (one CTA per SM, persistent).
-// Sweep 1 streams the row from HBM with an L2 evict-last policy and keeps online
-// (max, sum exp, sum x) per thread; sweep 2 re-reads the row -- it is still in L2, the
-// 148 rows in flight occupy ~37 MB -- with evict-first and writes the gradient with
-// evict-first stores, so HBM sees one read and one write per element.
+// Thread 0 keeps the next row in flight with an asynchronous bulk prefetch into L2
+// (evict-last), so HBM streams independently of the sweeps.  Sweep 1 reads the row and
+// keeps online (max, sum exp, sum x) per thread; sweep 2 re-reads it -- still in L2: the
+// rows in flight occupy ~2 x 148 x 250 KB -- with evict-first and writes the gradient
+// with evict-first stores, so HBM sees one read and one write per element.
 __device__ __forceinline__ uint64_t policy_evict_last() {
   uint64_t p;
   asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
@@ -402,6 +206,17 @@ __device__ __forceinline__ void st_hint(void* ptr, uint4 v, uint64_t pol) {
                : "memory");
 }
 
+// Asynchronous prefetch of a whole row into L2 (cp.async.bulk.prefetch), evict-last.
+__device__ __forceinline__ void prefetch_row(const void* src, uint32_t bytes, uint64_t pol) {
+  const char* p = static_cast<const char*>(src);
+  for (uint32_t off = 0; off < bytes; off += 65536u) {
+    const uint32_t n = bytes - off < 65536u ? bytes - off : 65536u;
+    asm volatile("cp.async.bulk.prefetch.L2.global.L2::cache_hint [%0], %1, %2;" ::"l"(p + off),
+                 "r"(n), "l"(pol)
+                 : "memory");
+  }
+}
+
 constexpr int kRowThreads = 1024;
 constexpr int kRowUnroll = 4;
 
@@ -420,9 +235,14 @@ __global__ void __launch_bounds__(kRowThreads, 1) ce_row_kernel(
   const float inv_nv = 1.0f / (float)(*n_valid_p);
   const float smooth = lsm / (float)n_cols;
   const float sub = smooth * inv_nv, hsub = (1.0f - lsm) * inv_nv;
+  const uint32_t row_bytes = (uint32_t)((int64_t)nvec * 16);
+  if (tid == 0 && blockIdx.x < n_rows) prefetch_row(logits + (int64_t)blockIdx.x * lstride, row_bytes, keep);
   for (int64_t row = blockIdx.x; row < n_rows; row += gridDim.x) {
     const T* src = logits + row * lstride;
     const int64_t t = targets[row];
+    // Keep the next row's HBM read in flight (into L2) while this row is processed.
+    if (tid == 0 && row + (int64_t)gridDim.x < n_rows)
+      prefetch_row(logits + (row + (int64_t)gridDim.x) * lstride, row_bytes, keep);
     Online o{-INFINITY, 0.f, 0.f};
     int v = tid;
     for (; v + (kRowUnroll - 1) * kRowThreads < nvec; v += kRowUnroll * kRowThreads) {
@@ -609,55 +429,14 @@ int fwd_t(const void* logits, int64_t ls, void* grad, int64_t gs, const int64_t*
   int s0 = launch_status("fk_ce_fwd(prologue)");
   if (s0 != FK_OK) return s0;
   if (n_rows > 0) {
-    constexpr int VN = 16 / sizeof(T);
-    int C = 1;
-    auto slice = [&](int c) {
-      int64_t per = (n_cols + c - 1) / c;
-      return ((per + VN - 1) / VN) * VN;
-    };
-    while (C < 8 && slice(C) * (int64_t)sizeof(T) > kMaxClusterBytes) C <<= 1;
-    const int64_t chunk = slice(C);
     const int rowvec = aligned16(lp) && aligned16(gp) && ((ls * (int64_t)sizeof(T)) % 16 == 0) &&
                        ((gs * (int64_t)sizeof(T)) % 16 == 0);
-    const char* path = getenv("FKB200_CE_PATH");
-    const bool use_row = rowvec && !(path && path[0] == 'c');
-    if (use_row) {
+    if (rowvec) {
       int64_t g = n_rows < (int64_t)num_sms() ? n_rows : (int64_t)num_sms();
       ce_row_kernel<T><<<(int)g, kRowThreads, 0, st>>>(lp, ls, gp, gs, targets, n_rows, (int)n_cols,
                                                        ignore, lsm, n_valid, loss_rows, err);
       int s1 = launch_status("fk_ce_fwd(row)");
       if (s1 != FK_OK) return s1;
-    } else if (chunk * (int64_t)sizeof(T) <= kMaxSliceBytes) {
-      const int smem = (int)(2 * chunk * sizeof(T));
-      auto kern = ce_cluster_kernel<T>;
-      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-      cudaLaunchConfig_t cfg = {};
-      cudaLaunchAttribute attr[1];
-      attr[0].id = cudaLaunchAttributeClusterDimension;
-      attr[0].val.clusterDim.x = C;
-      attr[0].val.clusterDim.y = 1;
-      attr[0].val.clusterDim.z = 1;
-      cfg.attrs = attr;
-      cfg.numAttrs = 1;
-      cfg.blockDim = dim3(kCeThreads);
-      cfg.dynamicSmemBytes = smem;
-      cfg.stream = st;
-      int max_clusters = 0;
-      cfg.gridDim = dim3(C * num_sms());
-      if (cudaOccupancyMaxActiveClusters(&max_clusters, kern, &cfg) != cudaSuccess ||
-          max_clusters < 1) {
-        cudaGetLastError();
-        max_clusters = num_sms() / C;
-        if (max_clusters < 1) max_clusters = 1;
-      }
-      int64_t nclu = n_rows < max_clusters ? n_rows : max_clusters;
-      cfg.gridDim = dim3((unsigned)(nclu * C));
-      const int bulk = aligned16(lp) && ((ls * (int64_t)sizeof(T)) % 16 == 0);
-      const int gvec = aligned16(gp) && ((gs * (int64_t)sizeof(T)) % 16 == 0);
-      cudaError_t e = cudaLaunchKernelEx(&cfg, kern, lp, ls, gp, gs, targets, n_rows, (int)n_cols,
-                                         ignore, lsm, (const int*)n_valid, loss_rows, err,
-                                         (int)chunk, bulk, gvec);
-      if (e != cudaSuccess) return fail(FK_ERR_LAUNCH, "fk_ce_fwd: %s", cudaGetErrorString(e));
     } else {
       int64_t g = n_rows < (int64_t)num_sms() * 4 ? n_rows : (int64_t)num_sms() * 4;
       ce_generic_kernel<T><<<(int)g, kCeThreads, 0, st>>>(lp, ls, gp, gs, targets, n_rows, n_cols,

@@ -109,12 +109,12 @@ __global__ void __launch_bounds__(kMetaThreads) moe_scatter_kernel(
     float* __restrict__ sorted_w, int* __restrict__ slot_pos) {
   __shared__ int run[kMaxExperts];
   __shared__ int wc[kMetaWarps][kMaxExperts];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
   for (int e = threadIdx.x; e < E; e += kMetaThreads) run[e] = part[(int64_t)blockIdx.x * E + e];
   const int64_t a0 = (int64_t)blockIdx.x * chunk;
   const int64_t a1 = a0 + chunk < n_assign ? a0 + chunk : n_assign;
   for (int64_t r0 = a0; r0 < a1; r0 += kMetaThreads) {
-    for (int i = threadIdx.x; i < kMetaWarps * E; i += kMetaThreads) (&wc[0][0])[i] = 0;
+    for (int i = threadIdx.x; i < kMetaWarps * E; i += kMetaThreads) wc[i / E][i % E] = 0;
     __syncthreads();
     const int64_t a = r0 + threadIdx.x;
     int e = -1;

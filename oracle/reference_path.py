@@ -136,15 +136,16 @@ def moe_layer_oracle(x, router_logits, w_gate, w_up, w_down, k, dout=None, dtype
     req = dout is not None
     X = x.detach().to(dtype).cpu().requires_grad_(req)
     L = router_logits.detach().to(dtype).cpu().requires_grad_(req)
-    Wg = w_gate.detach().to(dtype).cpu().requires_grad_(req)
-    Wu = w_up.detach().to(dtype).cpu().requires_grad_(req)
-    Wd = w_down.detach().to(dtype).cpu().requires_grad_(req)
+    E = w_gate.shape[0]
+    # one leaf per expert matrix, as the reference's ModuleList of Linear layers holds them
+    Wg = [w_gate[e].detach().to(dtype).cpu().requires_grad_(req) for e in range(E)]
+    Wu = [w_up[e].detach().to(dtype).cpu().requires_grad_(req) for e in range(E)]
+    Wd = [w_down[e].detach().to(dtype).cpu().requires_grad_(req) for e in range(E)]
     _, idx = route_oracle(router_logits, k)
     probs = torch.softmax(L, dim=-1)
     wsel = torch.gather(probs, 1, idx)
     wsel = wsel / wsel.sum(dim=-1, keepdim=True)
     out = torch.zeros_like(X)
-    E = Wg.shape[0]
     for e in range(E):
         match = idx == e
         tok = match.any(dim=-1)
@@ -157,7 +158,11 @@ def moe_layer_oracle(x, router_logits, w_gate, w_up, w_down, k, dout=None, dtype
     if not req:
         return out.detach()
     out.backward(dout.detach().to(dtype).cpu())
-    return out.detach(), X.grad, Wg.grad, Wu.grad, Wd.grad, L.grad
+
+    def stacked(ws):
+        return torch.stack([w.grad if w.grad is not None else torch.zeros_like(w) for w in ws])
+
+    return out.detach(), X.grad, stacked(Wg), stacked(Wu), stacked(Wd), L.grad
 
 
 def relative_error(a: torch.Tensor, b: torch.Tensor) -> float:
