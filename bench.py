@@ -676,6 +676,11 @@ def run_ours(args):
     wl = Router(args.router_rows) if args.workload == "router" else WORKLOADS[args.workload]()
     if args.rows and hasattr(wl, "rows") and args.workload != "router":
         wl.rows = args.rows
+    if args.workload == "moe":
+        if args.moe_tokens:
+            wl.tokens = args.moe_tokens
+        if args.moe_experts:
+            wl.E = args.moe_experts
     wl.setup(dev)
     stream = torch.cuda.current_stream(dev)
     pk = peaks()
@@ -863,6 +868,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="rmsnorm")
     ap.add_argument("--router-rows", type=int, default=4096)
+    ap.add_argument("--moe-tokens", type=int, default=0, help="profiling runs only")
+    ap.add_argument("--moe-experts", type=int, default=0, help="profiling runs only")
     ap.add_argument("--rows", type=int, default=0,
                     help="override the row count of rmsnorm/swiglu/ce (profiling runs only)")
     ap.add_argument("--no-cpu-baseline", action="store_true")

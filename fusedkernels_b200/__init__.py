@@ -8,8 +8,10 @@ from .cross_entropy import fused_cross_entropy
 from .rmsnorm import FusedRMSNorm
 from .swiglu import fused_swiglu
 from .moe_routing_v2 import fused_moe_route_v2
+from .moe_layer_sorted import FusedMoEMLPSorted
 
 __all__ = [
     "fused_cross_entropy", "FusedRMSNorm", "fused_swiglu", "fused_moe_route_v2",
+    "FusedMoEMLPSorted",
 ]
 __version__ = "0.2.0+b200"

@@ -1,14 +1,14 @@
 // Fused cross-entropy forward + gradient, reference cross_entropy.py:24-116.
 //
 // HBM traffic is one read of the logits and one write of the gradient.  A row of V
-// logits (250.5 KiB for V=128256 bf16) is larger than one SM's shared memory; instead of
-// splitting it across CTAs, one persistent CTA of 1024 threads per SM owns a row and
-// sweeps it twice: the first sweep reduces it to (max, sum exp, sum x) with an online
-// rescale, the second writes the gradient.  Both sweeps read from L2: the row is brought
-// in by an asynchronous bulk prefetch (cp.async.bulk.prefetch.L2, evict-last policy)
-// issued one row ahead, so the HBM read is the prefetch alone and overlaps the sweeps
-// of earlier rows.  Exponentials of 16-bit inputs are single ex2 instructions with
-// log2(e) folded into an FMA.
+// logits (250.5 KiB for V=128256 bf16) is larger than one SM's shared memory; one
+// persistent CTA of 1024 threads per SM owns a row and sweeps it twice: the first sweep
+// streams the row through a ring of shared-memory chunks filled by cp.async.bulk and
+// reduces it to (max, sum exp, sum x) with an online rescale; the second re-reads it from
+// L2 (the chunks were copied with an evict-last policy) and writes the gradient.  The
+// ring runs ahead across rows, so the next row's HBM read overlaps the second sweep.
+// Exponentials of 16-bit inputs are single ex2 instructions with log2(e) folded into an
+// FMA.
 //
 // The mean-reduction scale 1/n_valid is folded into the gradient write (n_valid comes
 // from a one-CTA prologue that counts non-ignored targets), and the scalar loss is a
@@ -177,12 +177,13 @@ __device__ __forceinline__ Online warp_combine(Online o) {
   return o;
 }
 
-// Two-sweep row kernel: one CTA of 1024 threads per row (one CTA per SM, persistent).
-// Thread 0 keeps the next row in flight with an asynchronous bulk prefetch into L2
-// (evict-last), so HBM streams independently of the sweeps.  Sweep 1 reads the row and
-// keeps online (max, sum exp, sum x) per thread; sweep 2 re-reads it -- still in L2: the
-// rows in flight occupy ~2 x 148 x 250 KB -- with evict-first and writes the gradient
-// with evict-first stores, so HBM sees one read and one write per element.
+// Two-sweep row kernel: one CTA of 1024 threads per SM, persistent over rows.
+// Sweep 1 consumes the row from a ring of kRingStages shared-memory chunks filled by
+// cp.async.bulk (thread 0 keeps the ring full, running ahead across row boundaries, so
+// the next row's HBM read overlaps this row's second sweep) and keeps online
+// (max, sum exp, sum x) per thread.  Sweep 2 re-reads the row from L2 -- the chunks were
+// copied with an evict-last policy moments earlier -- and writes the gradient with
+// evict-first stores, so HBM sees one read and one write per element.
 __device__ __forceinline__ uint64_t policy_evict_last() {
   uint64_t p;
   asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
@@ -205,20 +206,19 @@ __device__ __forceinline__ void st_hint(void* ptr, uint4 v, uint64_t pol) {
                "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w), "l"(pol)
                : "memory");
 }
-
-// Asynchronous prefetch of a whole row into L2 (cp.async.bulk.prefetch), evict-last.
-__device__ __forceinline__ void prefetch_row(const void* src, uint32_t bytes, uint64_t pol) {
-  const char* p = static_cast<const char*>(src);
-  for (uint32_t off = 0; off < bytes; off += 65536u) {
-    const uint32_t n = bytes - off < 65536u ? bytes - off : 65536u;
-    asm volatile("cp.async.bulk.prefetch.L2.global.L2::cache_hint [%0], %1, %2;" ::"l"(p + off),
-                 "r"(n), "l"(pol)
-                 : "memory");
-  }
+__device__ __forceinline__ void bulk_g2s_hint(void* dst, const void* src, uint32_t bytes,
+                                              uint64_t* bar, uint64_t pol) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1], %2, [%3], %4;" ::"r"(ptx::smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(ptx::smem_u32(bar)), "l"(pol)
+      : "memory");
 }
 
 constexpr int kRowThreads = 1024;
 constexpr int kRowUnroll = 4;
+constexpr int kRingStages = 6;
+constexpr int kChunkPackets = 2048;  // 32 KB per stage: two 16-byte packets per thread
 
 template <typename T>
 __global__ void __launch_bounds__(kRowThreads, 1) ce_row_kernel(
@@ -227,35 +227,74 @@ __global__ void __launch_bounds__(kRowThreads, 1) ce_row_kernel(
     float lsm, const int* __restrict__ n_valid_p, float* __restrict__ loss_rows,
     int* __restrict__ err) {
   constexpr int VN = 16 / sizeof(T);
+  extern __shared__ __align__(128) unsigned char ring[];
+  __shared__ __align__(8) uint64_t full[kRingStages], empty[kRingStages];
   __shared__ float wred[3][32];
-  __shared__ float stats[2];
+  __shared__ float stats[1];
+  __shared__ int dead;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int nvec = n_cols / VN;
+  const int nchunk = (nvec + kChunkPackets - 1) / kChunkPackets;
   const uint64_t keep = policy_evict_last(), drop = policy_evict_first();
   const float inv_nv = 1.0f / (float)(*n_valid_p);
   const float smooth = lsm / (float)n_cols;
   const float sub = smooth * inv_nv, hsub = (1.0f - lsm) * inv_nv;
-  const uint32_t row_bytes = (uint32_t)((int64_t)nvec * 16);
-  if (tid == 0 && blockIdx.x < n_rows) prefetch_row(logits + (int64_t)blockIdx.x * lstride, row_bytes, keep);
-  for (int64_t row = blockIdx.x; row < n_rows; row += gridDim.x) {
+  const int64_t G = gridDim.x;
+  const int64_t my_rows = blockIdx.x < n_rows ? (n_rows - 1 - blockIdx.x) / G + 1 : 0;
+  const int64_t total_chunks = my_rows * nchunk;
+
+  // Producer state (thread 0): next chunk to issue.
+  int64_t q_issue = 0;
+  auto issue = [&](int64_t q) {
+    const int64_t row = blockIdx.x + (q / nchunk) * G;
+    const int c = (int)(q % nchunk);
+    const int s = (int)(q % kRingStages);
+    const int pk = (nvec - c * kChunkPackets) < kChunkPackets ? nvec - c * kChunkPackets : kChunkPackets;
+    const uint32_t bytes = (uint32_t)pk * 16u;
+    ptx::mbar_arrive_expect_tx(&full[s], bytes);
+    bulk_g2s_hint(ring + (size_t)s * kChunkPackets * 16,
+                  logits + row * lstride + (int64_t)c * kChunkPackets * VN, bytes, &full[s], keep);
+  };
+  if (tid == 0) {
+    for (int s = 0; s < kRingStages; ++s) {
+      ptx::mbar_init(&full[s], 1);
+      ptx::mbar_init(&empty[s], kRowThreads / 32);
+    }
+    ptx::fence_mbar_init();
+    dead = 0;
+  }
+  __syncthreads();
+  if (tid == 0)
+    for (; q_issue < total_chunks && q_issue < kRingStages; ++q_issue) issue(q_issue);
+
+  int64_t q = 0;  // consumer chunk counter
+  for (int64_t row = blockIdx.x; row < n_rows; row += G) {
     const T* src = logits + row * lstride;
     const int64_t t = targets[row];
-    // Keep the next row's HBM read in flight (into L2) while this row is processed.
-    if (tid == 0 && row + (int64_t)gridDim.x < n_rows)
-      prefetch_row(logits + (row + (int64_t)gridDim.x) * lstride, row_bytes, keep);
     Online o{-INFINITY, 0.f, 0.f};
-    int v = tid;
-    for (; v + (kRowUnroll - 1) * kRowThreads < nvec; v += kRowUnroll * kRowThreads) {
-      Vec16<T> p[kRowUnroll];
+    bool ok = true;
+    for (int c = 0; c < nchunk; ++c, ++q) {
+      const int s = (int)(q % kRingStages);
+      if (!dead && !ptx::mbar_wait(&full[s], (uint32_t)((q / kRingStages) & 1))) ok = false;
+      const int pk = (nvec - c * kChunkPackets) < kChunkPackets ? nvec - c * kChunkPackets : kChunkPackets;
+      const uint4* sv = reinterpret_cast<const uint4*>(ring + (size_t)s * kChunkPackets * 16);
 #pragma unroll
-      for (int u = 0; u < kRowUnroll; ++u) p[u].u = ld_hint(src + (int64_t)(v + u * kRowThreads) * VN, keep);
-#pragma unroll
-      for (int u = 0; u < kRowUnroll; ++u) online_add_packet<T>(o, p[u]);
-    }
-    for (; v < nvec; v += kRowThreads) {
-      Vec16<T> p;
-      p.u = ld_hint(src + (int64_t)v * VN, keep);
-      online_add_packet<T>(o, p);
+      for (int u = 0; u < kChunkPackets / kRowThreads; ++u) {
+        const int v = tid + u * kRowThreads;
+        if (v < pk) {
+          Vec16<T> p;
+          p.u = sv[v];
+          online_add_packet<T>(o, p);
+        }
+      }
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(&empty[s]);
+      if (tid == 0) {
+        // Refill this stage once every warp has released it.
+        if (!dead && !ptx::mbar_wait(&empty[s], (uint32_t)((q / kRingStages) & 1))) ok = false;
+        if (!ok) dead = 1;
+        if (!dead && q_issue < total_chunks) issue(q_issue++);
+      }
     }
     for (int i = nvec * VN + tid; i < n_cols; i += kRowThreads) online_add_scalar<T>(o, Elt<T>::to_f(src[i]));
     o = warp_combine<T>(o);
@@ -265,31 +304,29 @@ __global__ void __launch_bounds__(kRowThreads, 1) ce_row_kernel(
       wred[2][warp] = o.sx;
     }
     __syncthreads();
+    const bool ignored = (t == ignore_index);
+    const bool invalid = !ignored && (t < 0 || t >= n_cols);
+    const bool poisoned = dead != 0;
     if (warp == 0) {
-      Online c{wred[0][lane], wred[1][lane], wred[2][lane]};
-      c = warp_combine<T>(c);
+      Online cc{wred[0][lane], wred[1][lane], wred[2][lane]};
+      cc = warp_combine<T>(cc);
       if (lane == 0) {
-        const float lse = c.m + logf(c.s);
+        const float lse = cc.m + logf(cc.s);
         stats[0] = lse;
-        const bool ignored = (t == ignore_index);
-        const bool invalid = !ignored && (t < 0 || t >= n_cols);
         float loss = invalid ? 0.f : lse - Elt<T>::to_f(src[ignored ? 0 : t]);
-        if (lsm > 0.f) loss = (1.0f - lsm) * loss + lsm * (lse - c.sx / (float)n_cols);
+        if (lsm > 0.f) loss = (1.0f - lsm) * loss + lsm * (lse - cc.sx / (float)n_cols);
         if (ignored) loss = 0.f;
-        if (invalid) {
-          loss = __int_as_float(0x7fc00000);
-          atomicExch(err, 1);
-        }
+        if (invalid || poisoned) loss = __int_as_float(0x7fc00000);
+        if (invalid) atomicExch(err, 1);
+        if (poisoned) atomicExch(err, 2);
         loss_rows[row] = loss;
       }
     }
     __syncthreads();
     const float lse = stats[0];
-    const bool ignored = (t == ignore_index);
-    const bool invalid = !ignored && (t < 0 || t >= n_cols);
     T* dst = grad + row * gstride;
-    if (ignored || invalid) {
-      const T z = Elt<T>::from_f(invalid ? __int_as_float(0x7fc00000) : 0.f);
+    if (ignored || invalid || poisoned) {
+      const T z = Elt<T>::from_f((invalid || poisoned) ? __int_as_float(0x7fc00000) : 0.f);
       Vec16<T> zz;
 #pragma unroll
       for (int e = 0; e < VN; ++e) zz.e[e] = z;
@@ -302,35 +339,28 @@ __global__ void __launch_bounds__(kRowThreads, 1) ce_row_kernel(
         else return ex2f(fmaf(x, kLog2e, -cexp)) - sub;
       };
       const int tv = (int)(t / VN);
+      auto emit = [&](int vv, const Vec16<T>& p) {
+        float g[VN];
+#pragma unroll
+        for (int e = 0; e < VN; ++e) g[e] = gval(Elt<T>::to_f(p.e[e]));
+        if (vv == tv && t < (int64_t)nvec * VN) g[t - (int64_t)vv * VN] -= hsub;
+        Vec16<T> o2;
+#pragma unroll
+        for (int e = 0; e < VN; ++e) o2.e[e] = Elt<T>::from_f(g[e]);
+        st_hint(dst + (int64_t)vv * VN, o2.u, drop);
+      };
       int w = tid;
       for (; w + (kRowUnroll - 1) * kRowThreads < nvec; w += kRowUnroll * kRowThreads) {
         Vec16<T> p[kRowUnroll];
 #pragma unroll
         for (int u = 0; u < kRowUnroll; ++u) p[u].u = ld_hint(src + (int64_t)(w + u * kRowThreads) * VN, drop);
 #pragma unroll
-        for (int u = 0; u < kRowUnroll; ++u) {
-          const int vv = w + u * kRowThreads;
-          float g[VN];
-#pragma unroll
-          for (int e = 0; e < VN; ++e) g[e] = gval(Elt<T>::to_f(p[u].e[e]));
-          if (vv == tv && t < (int64_t)nvec * VN) g[t - (int64_t)vv * VN] -= hsub;
-          Vec16<T> o2;
-#pragma unroll
-          for (int e = 0; e < VN; ++e) o2.e[e] = Elt<T>::from_f(g[e]);
-          st_hint(dst + (int64_t)vv * VN, o2.u, drop);
-        }
+        for (int u = 0; u < kRowUnroll; ++u) emit(w + u * kRowThreads, p[u]);
       }
       for (; w < nvec; w += kRowThreads) {
         Vec16<T> p;
         p.u = ld_hint(src + (int64_t)w * VN, drop);
-        float g[VN];
-#pragma unroll
-        for (int e = 0; e < VN; ++e) g[e] = gval(Elt<T>::to_f(p.e[e]));
-        if (w == tv && t < (int64_t)nvec * VN) g[t - (int64_t)w * VN] -= hsub;
-        Vec16<T> o2;
-#pragma unroll
-        for (int e = 0; e < VN; ++e) o2.e[e] = Elt<T>::from_f(g[e]);
-        st_hint(dst + (int64_t)w * VN, o2.u, drop);
+        emit(w, p);
       }
       for (int i = nvec * VN + tid; i < n_cols; i += kRowThreads) {
         float g = gval(Elt<T>::to_f(src[i]));
@@ -338,7 +368,7 @@ __global__ void __launch_bounds__(kRowThreads, 1) ce_row_kernel(
         dst[i] = Elt<T>::from_f(g);
       }
     }
-    __syncthreads();  // in-place: every read of this row precedes the next row's stats
+    __syncthreads();  // in-place: every read of this row precedes later rows' writes
   }
 }
 
@@ -433,8 +463,11 @@ int fwd_t(const void* logits, int64_t ls, void* grad, int64_t gs, const int64_t*
                        ((gs * (int64_t)sizeof(T)) % 16 == 0);
     if (rowvec) {
       int64_t g = n_rows < (int64_t)num_sms() ? n_rows : (int64_t)num_sms();
-      ce_row_kernel<T><<<(int)g, kRowThreads, 0, st>>>(lp, ls, gp, gs, targets, n_rows, (int)n_cols,
-                                                       ignore, lsm, n_valid, loss_rows, err);
+      const int smem = kRingStages * kChunkPackets * 16;
+      cudaFuncSetAttribute(ce_row_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+      ce_row_kernel<T><<<(int)g, kRowThreads, smem, st>>>(lp, ls, gp, gs, targets, n_rows,
+                                                          (int)n_cols, ignore, lsm, n_valid,
+                                                          loss_rows, err);
       int s1 = launch_status("fk_ce_fwd(row)");
       if (s1 != FK_OK) return s1;
     } else {
