@@ -44,6 +44,12 @@ SIGNATURES: dict[str, list] = {
     "fk_moe_gemm_down_dgrad": [_vp, _i64, _i32, _vp, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp],
     "fk_moe_gemm_up_dgrad": [_vp, _i64, _i32, _vp, _i32, _i32, _vp, _vp, _vp, _vp, _vp],
     "fk_moe_gemm_wgrad": [_vp, _i32, _vp, _i32, _i64, _vp, _i32, _vp, _vp, _vp],
+    "fk_moe_route_meta_skip": [_vp, _vp, _i64, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
+                               _i64, _vp, _sz, _vp, _vp],
+    "fk_ep_plan": [_vp, _vp, _i64, _i32, _vp, _vp, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp],
+    "fk_ep_pack": [_vp, _i32, _vp, _i64, _vp, _i32, _vp],
+    "fk_ep_unpack_sum": [_vp, _i32, _vp, _i64, _i32, _vp, _i32, _vp],
+    "fk_ep_unpack_dw": [_vp, _vp, _vp, _vp, _i64, _i32, _i32, _i32, _vp, _vp],
 }
 _RESTYPES = {"fk_status_string": C.c_char_p, "fk_last_error": C.c_char_p}
 

@@ -35,8 +35,11 @@ __device__ __forceinline__ uint32_t lanemask_lt() {
 }
 
 // Workspace: [G][E] int histograms (become base offsets), then one int ticket.
+// IDX is int64_t (router output) or int (expert-parallel receive buffers); with SKIP, a
+// negative id marks an unused slot instead of an error.
+template <typename IDX, bool SKIP>
 __global__ void __launch_bounds__(kMetaThreads) moe_hist_kernel(
-    const int64_t* __restrict__ idx, int64_t n_assign, int E, int64_t chunk,
+    const IDX* __restrict__ idx, int64_t n_assign, int E, int64_t chunk,
     int* __restrict__ part, unsigned int* __restrict__ ticket, int* __restrict__ counts,
     int* __restrict__ seg_start, int* __restrict__ tile_expert, int* __restrict__ n_mblk,
     int* __restrict__ sorted_assign, float* __restrict__ sorted_w, int64_t max_rows,
@@ -50,7 +53,7 @@ __global__ void __launch_bounds__(kMetaThreads) moe_hist_kernel(
   for (int64_t a = a0 + threadIdx.x; a < a1; a += kMetaThreads) {
     int64_t e = idx[a];
     if (e >= 0 && e < E) atomicAdd(&h[e], 1);
-    else atomicExch(err, 1);
+    else if (!SKIP || e >= E) atomicExch(err, 1);
   }
   __syncthreads();
   for (int e = threadIdx.x; e < E; e += kMetaThreads) part[(int64_t)blockIdx.x * E + e] = h[e];
@@ -103,8 +106,9 @@ __global__ void __launch_bounds__(kMetaThreads) moe_hist_kernel(
   if (threadIdx.x == 0) *ticket = 0u;  // ready for the next call
 }
 
+template <typename IDX>
 __global__ void __launch_bounds__(kMetaThreads) moe_scatter_kernel(
-    const int64_t* __restrict__ idx, const float* __restrict__ w, int64_t n_assign, int E,
+    const IDX* __restrict__ idx, const float* __restrict__ w, int64_t n_assign, int E,
     int64_t chunk, const int* __restrict__ part, int* __restrict__ sorted_assign,
     float* __restrict__ sorted_w, int* __restrict__ slot_pos) {
   __shared__ int run[kMaxExperts];
@@ -288,39 +292,62 @@ extern "C" int fk_moe_capacity(int64_t n_tokens, int k, int n_experts, int64_t* 
   return FK_OK;
 }
 
-extern "C" int fk_moe_route_meta(const int64_t* idx, const float* w, int64_t n_tokens, int k,
-                                 int n_experts, int* counts, int* seg_start, int* tile_expert,
-                                 int* n_mblk, int* sorted_assign, float* sorted_w,
-                                 int* slot_pos, int64_t max_rows, void* workspace,
-                                 size_t workspace_bytes, int* err_flag, void* stream) {
-  FK_CHECK_ARG(n_tokens >= 0 && k >= 1 && n_experts >= 1 && n_experts <= fk::kMaxExperts,
+namespace fk {
+template <typename IDX, bool SKIP>
+static int route_meta_t(const IDX* idx, const float* w, int64_t n_tokens, int k, int n_experts,
+                        int* counts, int* seg_start, int* tile_expert, int* n_mblk,
+                        int* sorted_assign, float* sorted_w, int* slot_pos, int64_t max_rows,
+                        void* workspace, size_t workspace_bytes, int* err_flag, void* stream) {
+  FK_CHECK_ARG(n_tokens >= 0 && k >= 1 && n_experts >= 1 && n_experts <= kMaxExperts,
                "fk_moe_route_meta: bad sizes");
   FK_CHECK_ARG(counts && seg_start && tile_expert && n_mblk && sorted_assign && sorted_w &&
                    err_flag && (n_tokens == 0 || (idx && w && slot_pos)),
                "fk_moe_route_meta: null pointer");
-  FK_CHECK_ARG(max_rows >= fk::moe_capacity_rows(n_tokens, k, n_experts),
+  FK_CHECK_ARG(max_rows >= moe_capacity_rows(n_tokens, k, n_experts),
                "fk_moe_route_meta: max_rows %lld below capacity", (long long)max_rows);
-  const size_t need = fk::moe_meta_ws_bytes(n_tokens, k, n_experts);
+  const size_t need = moe_meta_ws_bytes(n_tokens, k, n_experts);
   if (!workspace || workspace_bytes < need)
-    return fk::fail(FK_ERR_WORKSPACE, "fk_moe_route_meta: need %zu workspace bytes", need);
-  cudaStream_t st = fk::as_stream(stream);
+    return fail(FK_ERR_WORKSPACE, "fk_moe_route_meta: need %zu workspace bytes", need);
+  cudaStream_t st = as_stream(stream);
   const int64_t n_assign = n_tokens * k;
-  const int G = fk::meta_grid(n_assign);
+  const int G = meta_grid(n_assign);
   const int64_t chunk = (n_assign + G - 1) / G;
   int* part = static_cast<int*>(workspace);
   unsigned int* ticket = reinterpret_cast<unsigned int*>(part + (size_t)G * n_experts);
   // The ticket must start at zero; the kernel's last CTA resets it after every call.
   cudaMemsetAsync(ticket, 0, sizeof(unsigned int), st);
   cudaMemsetAsync(err_flag, 0, sizeof(int), st);
-  fk::moe_hist_kernel<<<G, fk::kMetaThreads, 0, st>>>(idx, n_assign, n_experts, chunk < 1 ? 1 : chunk,
-                                                      part, ticket, counts, seg_start, tile_expert,
-                                                      n_mblk, sorted_assign, sorted_w, max_rows,
-                                                      err_flag);
-  int s = fk::launch_status("fk_moe_route_meta(hist)");
+  moe_hist_kernel<IDX, SKIP><<<G, kMetaThreads, 0, st>>>(idx, n_assign, n_experts,
+                                                        chunk < 1 ? 1 : chunk, part, ticket, counts,
+                                                        seg_start, tile_expert, n_mblk,
+                                                        sorted_assign, sorted_w, max_rows, err_flag);
+  int s = launch_status("fk_moe_route_meta(hist)");
   if (s != FK_OK || n_assign == 0) return s;
-  fk::moe_scatter_kernel<<<G, fk::kMetaThreads, 0, st>>>(idx, w, n_assign, n_experts, chunk, part,
-                                                         sorted_assign, sorted_w, slot_pos);
-  return fk::launch_status("fk_moe_route_meta(scatter)");
+  moe_scatter_kernel<IDX><<<G, kMetaThreads, 0, st>>>(idx, w, n_assign, n_experts, chunk, part,
+                                                      sorted_assign, sorted_w, slot_pos);
+  return launch_status("fk_moe_route_meta(scatter)");
+}
+}  // namespace fk
+
+extern "C" int fk_moe_route_meta(const int64_t* idx, const float* w, int64_t n_tokens, int k,
+                                 int n_experts, int* counts, int* seg_start, int* tile_expert,
+                                 int* n_mblk, int* sorted_assign, float* sorted_w,
+                                 int* slot_pos, int64_t max_rows, void* workspace,
+                                 size_t workspace_bytes, int* err_flag, void* stream) {
+  return fk::route_meta_t<int64_t, false>(idx, w, n_tokens, k, n_experts, counts, seg_start,
+                                          tile_expert, n_mblk, sorted_assign, sorted_w, slot_pos,
+                                          max_rows, workspace, workspace_bytes, err_flag, stream);
+}
+
+extern "C" int fk_moe_route_meta_skip(const int* idx, const float* w, int64_t n_tokens, int k,
+                                      int n_experts, int* counts, int* seg_start,
+                                      int* tile_expert, int* n_mblk, int* sorted_assign,
+                                      float* sorted_w, int* slot_pos, int64_t max_rows,
+                                      void* workspace, size_t workspace_bytes, int* err_flag,
+                                      void* stream) {
+  return fk::route_meta_t<int, true>(idx, w, n_tokens, k, n_experts, counts, seg_start,
+                                     tile_expert, n_mblk, sorted_assign, sorted_w, slot_pos,
+                                     max_rows, workspace, workspace_bytes, err_flag, stream);
 }
 
 extern "C" int fk_moe_gather(const void* x, int dim, const int* sorted_assign, int k,

@@ -1,0 +1,279 @@
+"""Expert-parallel sorted-dispatch MoE layer (one process per GPU, NCCL over NVLink).
+
+The reference runs every expert on one GPU (fusedkernels/moe_layer_sorted.py:37); this
+module shards the experts of ``FusedMoEMLPSorted`` across the ranks of a process group
+(16 experts per GPU for E=128 on 8 GPUs) and exchanges token rows with all-to-all:
+
+  forward   route locally -> fk_ep_plan (which ranks need each token, deduplicated) ->
+            fk_ep_pack -> all-to-all of rows and slot metadata -> local grouped-GEMM
+            experts on the received rows -> per-row pre-reduction of the local slots ->
+            all-to-all back -> fk_ep_unpack_sum (rank-ordered sum: deterministic)
+  backward  the mirror image: dout rows out, per-slot routing gradients and partial input
+            gradients back; the input-gradient all-to-all runs concurrently with the
+            weight-gradient GEMMs.
+
+Every (source, destination) pair has a fixed capacity of T rows (a token is sent at most
+once per destination), so all collectives have static sizes: no host synchronisation and
+no split-size exchange.  Expert placement is static and load-aware: ``lpt_placement``
+bin-packs experts, hottest first, onto the least-loaded rank with a free slot.
+
+``ExpertParallelMoEMLP`` keeps the reference's parameter naming for the experts it holds
+(``experts.<global id>.w_gate.weight`` ...) and a replicated ``router``.  Gradients of the
+replicated router weight are local; averaging them across data-parallel ranks is the
+caller's job (``allreduce_router_grad``).
+"""
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+import torch.nn as nn
+
+from . import _lib
+from .moe_layer import Expert
+from .moe_layer_sorted import _Plan
+from .moe_routing_v2 import fused_moe_route_v2
+
+
+def lpt_placement(load, n_ranks: int) -> list[int]:
+    """Static expert -> rank map with exactly E/n_ranks experts per rank, balancing the
+    given per-expert load: experts in descending load order go to the least-loaded rank
+    that still has a free slot (longest-processing-time-first bin packing)."""
+    load = [float(v) for v in load]
+    E = len(load)
+    if E % n_ranks:
+        raise ValueError(f"n_experts={E} is not divisible by n_ranks={n_ranks}")
+    cap = E // n_ranks
+    tot = [0.0] * n_ranks
+    used = [0] * n_ranks
+    rank_of = [0] * E
+    for e in sorted(range(E), key=lambda i: (-load[i], i)):
+        r = min((r for r in range(n_ranks) if used[r] < cap), key=lambda r: (tot[r], r))
+        rank_of[e] = r
+        tot[r] += load[e]
+        used[r] += 1
+    return rank_of
+
+
+def round_robin_placement(n_experts: int, n_ranks: int) -> list[int]:
+    return [e % n_ranks for e in range(n_experts)]
+
+
+class Exchange:
+    """Fixed-capacity all-to-all of [n_ranks * cap, ...] buffers over a process group."""
+
+    def __init__(self, group=None):
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+
+    def all_to_all(self, send: torch.Tensor, async_op: bool = False):
+        recv = torch.empty_like(send)
+        work = dist.all_to_all_single(recv, send, group=self.group, async_op=async_op)
+        return (recv, work) if async_op else recv
+
+
+def _pack_meta(e: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+    """[rows, k] int32 expert ids + [rows, k] fp32 weights -> one [rows, 2k] int32 tensor."""
+    return torch.cat([e, w.view(torch.int32)], dim=1)
+
+
+def _unpack_meta(m: torch.Tensor, k: int):
+    return m[:, :k].contiguous(), m[:, k:].contiguous().view(torch.float32)
+
+
+class _EPMoEFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, w, idx, layer, *expert_params):
+        T, d = x.shape
+        k = idx.shape[1]
+        ex = layer.exchange
+        N = ex.world
+        El, H, E = len(layer.local_ids), layer.hidden_dim, layer.n_experts
+        dev = x.device
+        st = _lib.stream_of(x)
+        i32 = dict(dtype=torch.int32, device=dev)
+        idx = idx.contiguous()
+        w = w.to(torch.float32).contiguous()
+        send_token = torch.empty(N * T, **i32)
+        send_e = torch.empty(N * T, k, **i32)
+        send_w = torch.empty(N * T, k, dtype=torch.float32, device=dev)
+        src_pos = torch.empty(T, N, **i32)
+        send_count = torch.empty(N, **i32)
+        perr = torch.zeros(1, **i32)
+        _lib.call("fk_ep_plan", idx.data_ptr(), w.data_ptr(), T, k, layer.expert_rank.data_ptr(),
+                  layer.expert_local.data_ptr(), E, N, send_token.data_ptr(), send_e.data_ptr(),
+                  send_w.data_ptr(), src_pos.data_ptr(), send_count.data_ptr(), perr.data_ptr(), st)
+        send_x = torch.empty(N * T, d, dtype=torch.bfloat16, device=dev)
+        _lib.call("fk_ep_pack", x.data_ptr(), d, send_token.data_ptr(), N * T, send_x.data_ptr(),
+                  _lib.FK_BF16, st)
+        recv_x = ex.all_to_all(send_x)
+        recv_e, recv_w = _unpack_meta(ex.all_to_all(_pack_meta(send_e, send_w)), k)
+        # local experts on the received rows (N*T "tokens" with k slots, -1 = not local)
+        R_tok = N * T
+        plan = _Plan(R_tok, k, El, dev)
+        R = plan.max_rows
+        eptr = plan.err.data_ptr()
+        _lib.call("fk_moe_route_meta_skip", recv_e.data_ptr(), recv_w.data_ptr(), R_tok, k, El,
+                  plan.counts.data_ptr(), plan.seg_start.data_ptr(), plan.tile_expert.data_ptr(),
+                  plan.n_mblk.data_ptr(), plan.sorted_assign.data_ptr(), plan.sorted_w.data_ptr(),
+                  plan.slot_pos.data_ptr(), R, plan.ws.data_ptr(), plan.ws.numel(), eptr, st)
+        bf = dict(dtype=torch.bfloat16, device=dev)
+        xs = torch.empty(R, d, **bf)
+        h1 = torch.empty(R, 2 * H, **bf)
+        act = torch.empty(R, H, **bf)
+        y = torch.empty(R, d, **bf)
+        partial = torch.empty(R_tok, d, **bf)
+        _lib.call("fk_moe_gather", recv_x.data_ptr(), d, plan.sorted_assign.data_ptr(), k,
+                  plan.n_mblk.data_ptr(), R, xs.data_ptr(), _lib.FK_BF16, st)
+        _lib.call("fk_moe_gemm_up", xs.data_ptr(), R, d, layer.w13.data_ptr(), H, El,
+                  plan.tile_expert.data_ptr(), plan.n_mblk.data_ptr(), h1.data_ptr(),
+                  act.data_ptr(), eptr + 4, st)
+        _lib.call("fk_moe_gemm_down", act.data_ptr(), R, H, layer.w2.data_ptr(), d, El,
+                  plan.tile_expert.data_ptr(), plan.n_mblk.data_ptr(), y.data_ptr(), eptr + 4, st)
+        _lib.call("fk_moe_combine", y.data_ptr(), d, plan.slot_pos.data_ptr(), recv_w.data_ptr(),
+                  R_tok, k, partial.data_ptr(), _lib.FK_BF16, st)
+        back = ex.all_to_all(partial)
+        out = torch.empty(T, d, **bf)
+        _lib.call("fk_ep_unpack_sum", back.data_ptr(), d, src_pos.data_ptr(), T, N, out.data_ptr(),
+                  _lib.FK_BF16, st)
+        ctx.save_for_backward(xs, h1, act, y, idx, src_pos, send_token)
+        ctx.plan = plan
+        ctx.layer = layer
+        ctx.dims = (T, d, k, N, El, H, E)
+        return out
+
+    @staticmethod
+    def backward(ctx, dout):
+        xs, h1, act, y, idx, src_pos, send_token = ctx.saved_tensors
+        plan, layer = ctx.plan, ctx.layer
+        T, d, k, N, El, H, E = ctx.dims
+        ex = layer.exchange
+        dev = xs.device
+        st = _lib.stream_of(xs)
+        R = plan.max_rows
+        R_tok = N * T
+        eptr = plan.err.data_ptr()
+        bf = dict(dtype=torch.bfloat16, device=dev)
+        dout = dout.to(torch.bfloat16).contiguous()
+        send_d = torch.empty(R_tok, d, **bf)
+        _lib.call("fk_ep_pack", dout.data_ptr(), d, send_token.data_ptr(), R_tok, send_d.data_ptr(),
+                  _lib.FK_BF16, st)
+        recv_d = ex.all_to_all(send_d)
+        dy = torch.empty(R, d, **bf)
+        dw_recv = torch.zeros(R_tok, k, dtype=torch.float32, device=dev)
+        dh1 = torch.empty(R, 2 * H, **bf)
+        dxs = torch.empty(R, d, **bf)
+        dw13 = torch.empty(El, 2 * H, d, **bf)
+        dw2 = torch.empty(El, d, H, **bf)
+        dx_part = torch.empty(R_tok, d, **bf)
+        _lib.call("fk_moe_combine_bwd", recv_d.data_ptr(), y.data_ptr(), d,
+                  plan.sorted_assign.data_ptr(), plan.sorted_w.data_ptr(), k,
+                  plan.n_mblk.data_ptr(), R, dy.data_ptr(), dw_recv.data_ptr(), _lib.FK_BF16, st)
+        _lib.call("fk_moe_gemm_down_dgrad", dy.data_ptr(), R, d, layer.w2.data_ptr(), H, El,
+                  plan.tile_expert.data_ptr(), plan.n_mblk.data_ptr(), h1.data_ptr(),
+                  dh1.data_ptr(), eptr + 4, st)
+        _lib.call("fk_moe_gemm_up_dgrad", dh1.data_ptr(), R, H, layer.w13.data_ptr(), d, El,
+                  plan.tile_expert.data_ptr(), plan.n_mblk.data_ptr(), dxs.data_ptr(), eptr + 4, st)
+        _lib.call("fk_moe_combine", dxs.data_ptr(), d, plan.slot_pos.data_ptr(), None, R_tok, k,
+                  dx_part.data_ptr(), _lib.FK_BF16, st)
+        # input-gradient and routing-gradient exchange overlap the weight-gradient GEMMs
+        back_dx, w1 = ex.all_to_all(dx_part, async_op=True)
+        back_dw, w2 = ex.all_to_all(dw_recv, async_op=True)
+        _lib.call("fk_moe_gemm_wgrad", dy.data_ptr(), d, act.data_ptr(), H, R,
+                  plan.seg_start.data_ptr(), El, dw2.data_ptr(), eptr + 4, st)
+        _lib.call("fk_moe_gemm_wgrad", dh1.data_ptr(), 2 * H, xs.data_ptr(), d, R,
+                  plan.seg_start.data_ptr(), El, dw13.data_ptr(), eptr + 4, st)
+        w1.wait()
+        w2.wait()
+        dx = torch.empty(T, d, **bf)
+        _lib.call("fk_ep_unpack_sum", back_dx.data_ptr(), d, src_pos.data_ptr(), T, N,
+                  dx.data_ptr(), _lib.FK_BF16, st)
+        dw = torch.empty(T, k, dtype=torch.float32, device=dev)
+        _lib.call("fk_ep_unpack_dw", back_dw.data_ptr(), idx.data_ptr(),
+                  layer.expert_rank.data_ptr(), src_pos.data_ptr(), T, k, N, E, dw.data_ptr(), st)
+        grads = []
+        for e in range(El):
+            grads += [dw13[e, :H], dw13[e, H:], dw2[e]]
+        return (dx, dw, None, None, *grads)
+
+
+class ExpertParallelMoEMLP(nn.Module):
+    """``FusedMoEMLPSorted`` with its experts sharded over a process group (see module doc).
+
+    placement: expert -> rank list (default ``round_robin_placement``).  Every rank must
+    construct the layer with the same placement."""
+
+    def __init__(self, dim: int, hidden_dim: int, n_experts: int, k: int = 2, group=None,
+                 placement=None, router_version: str = "v2"):
+        super().__init__()
+        assert router_version == "v2"
+        self.dim, self.hidden_dim, self.n_experts, self.k = dim, hidden_dim, n_experts, k
+        self.exchange = Exchange(group)
+        N, r = self.exchange.world, self.exchange.rank
+        placement = list(placement) if placement is not None else round_robin_placement(n_experts, N)
+        assert len(placement) == n_experts and all(0 <= p < N for p in placement)
+        self.placement = placement
+        self.local_ids = [e for e in range(n_experts) if placement[e] == r]
+        local_of = {e: i for i, e in enumerate(self.local_ids)}
+        self.router = nn.Linear(dim, n_experts, bias=False)
+        self.experts = nn.ModuleDict({str(e): Expert(dim, hidden_dim) for e in self.local_ids})
+        self.register_buffer("expert_rank", torch.tensor(placement, dtype=torch.int32), persistent=False)
+        self.register_buffer("expert_local",
+                             torch.tensor([local_of.get(e, -1) for e in range(n_experts)],
+                                          dtype=torch.int32), persistent=False)
+        self._restack()
+
+    def _expert_params(self):
+        out = []
+        for e in self.local_ids:
+            ex = self.experts[str(e)]
+            out += [ex.w_gate.weight, ex.w_up.weight, ex.w_down.weight]
+        return out
+
+    def _restack(self):
+        El, H, D = len(self.local_ids), self.hidden_dim, self.dim
+        p0 = self.router.weight
+        with torch.no_grad():
+            w13 = torch.empty(El, 2 * H, D, dtype=p0.dtype, device=p0.device)
+            w2 = torch.empty(El, D, H, dtype=p0.dtype, device=p0.device)
+            for i, e in enumerate(self.local_ids):
+                ex = self.experts[str(e)]
+                w13[i, :H].copy_(ex.w_gate.weight)
+                w13[i, H:].copy_(ex.w_up.weight)
+                w2[i].copy_(ex.w_down.weight)
+                ex.w_gate.weight.data = w13[i, :H]
+                ex.w_up.weight.data = w13[i, H:]
+                ex.w_down.weight.data = w2[i]
+        self.w13, self.w2 = w13, w2
+
+    def _apply(self, fn, *args, **kwargs):
+        r = super()._apply(fn, *args, **kwargs)
+        self._restack()
+        return r
+
+    @torch.no_grad()
+    def load_from_full(self, router_weight, w_gate, w_up, w_down):
+        """Copy the router and this rank's experts out of full stacked weights
+        (w_gate, w_up [E, H, D], w_down [E, D, H])."""
+        self.router.weight.copy_(router_weight)
+        for i, e in enumerate(self.local_ids):
+            self.w13[i, :self.hidden_dim].copy_(w_gate[e])
+            self.w13[i, self.hidden_dim:].copy_(w_up[e])
+            self.w2[i].copy_(w_down[e])
+
+    def allreduce_router_grad(self):
+        g = self.router.weight.grad
+        if g is not None and self.exchange.world > 1:
+            dist.all_reduce(g, group=self.exchange.group)
+            g.div_(self.exchange.world)
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        assert x.is_cuda
+        orig_shape = x.shape
+        x_flat = x.reshape(-1, self.dim).contiguous()
+        if x_flat.dtype != torch.bfloat16 or self.w13.dtype != torch.bfloat16:
+            raise TypeError("ExpertParallelMoEMLP runs on bf16 tensor cores: use bfloat16")
+        logits = self.router(x_flat)
+        w, idx = fused_moe_route_v2(logits, self.k)
+        out = _EPMoEFn.apply(x_flat, w, idx, self, *self._expert_params())
+        return out.reshape(orig_shape)

@@ -193,6 +193,38 @@ FK_API int fk_moe_gemm_wgrad(const void* a, int m_dim, const void* b, int n_dim,
                              int64_t max_rows, const int* seg_start, int n_experts, void* dw,
                              int* err_flag, void* stream);
 
+/* Same as fk_moe_route_meta with int32 expert ids where a negative id marks an unused
+ * slot (expert-parallel receive buffers carry -1 for slots owned by other ranks). */
+FK_API int fk_moe_route_meta_skip(const int* idx, const float* w, int64_t n_tokens, int k,
+                                  int n_experts, int* counts, int* seg_start,
+                                  int* tile_expert, int* n_mblk, int* sorted_assign,
+                                  float* sorted_w, int* slot_pos, int64_t max_rows,
+                                  void* workspace, size_t workspace_bytes, int* err_flag,
+                                  void* stream);
+
+/* ---------------------------------------------------------------- expert parallelism
+ * No counterpart in the reference (its experts are all local, moe_layer_sorted.py:37).
+ * Each rank holds n_tokens local tokens; every (source, destination) pair has a fixed
+ * capacity of n_tokens rows, so the all-to-all buffers are [n_ranks * n_tokens, ...].
+ * fk_ep_plan: for every destination rank d, the stable list of local tokens with at least
+ *   one slot on d (send_token[d*T + i]), each row's k slot entries (send_e = d's local
+ *   expert id or -1, send_w = routing weight), src_pos[t*n_ranks + d] (row of token t in
+ *   d's list or -1) and send_count[d].  expert_rank/expert_local: [E] placement tables.
+ * fk_ep_pack: send_x[r, :] = x[send_token[r], :] (rows with no token are left untouched).
+ * fk_ep_unpack_sum: out[t, :] = sum_d back[d*T + src_pos[t, d], :] in rank order (fp32).
+ * fk_ep_unpack_dw: dw[t, j] = back_dw[(d*T + src_pos[t, d])*k + j], d = rank of idx[t, j]. */
+FK_API int fk_ep_plan(const int64_t* idx, const float* w, int64_t n_tokens, int k,
+                      const int* expert_rank, const int* expert_local, int n_experts,
+                      int n_ranks, int* send_token, int* send_e, float* send_w, int* src_pos,
+                      int* send_count, int* err_flag, void* stream);
+FK_API int fk_ep_pack(const void* x, int dim, const int* send_token, int64_t rows, void* send_x,
+                      int dtype, void* stream);
+FK_API int fk_ep_unpack_sum(const void* back, int dim, const int* src_pos, int64_t n_tokens,
+                            int n_ranks, void* out, int dtype, void* stream);
+FK_API int fk_ep_unpack_dw(const float* back_dw, const int64_t* idx, const int* expert_rank,
+                           const int* src_pos, int64_t n_tokens, int k, int n_ranks,
+                           int n_experts, float* dw, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,0 +1,182 @@
+"""Expert-parallel kernels and layer on the GPU.  The plan/pack/unpack kernels are checked
+bit-exactly (integers) and to fp32 rounding (sums) against tests/ep_reference.py for
+2 and 8 simulated ranks; the EP layer on a one-rank NCCL group must reproduce the
+single-GPU FusedMoEMLPSorted bit for bit; with two or more GPUs, a 2-rank run is checked
+against the single-GPU layer (2e-2 of max magnitude, bf16)."""
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+
+from fusedkernels_b200 import _lib
+from fusedkernels_b200.moe_ep import ExpertParallelMoEMLP, lpt_placement
+from fusedkernels_b200.moe_layer_sorted import FusedMoEMLPSorted
+from oracle import route_oracle
+from ep_reference import ep_plan, ep_unpack_dw, ep_unpack_sum
+from conftest import gen
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+@pytest.mark.parametrize("n_ranks,T,k,E", [(2, 300, 2, 8), (8, 1000, 8, 128), (8, 5, 2, 64)])
+def test_ep_plan_pack_unpack_match_reference(n_ranks, T, k, E):
+    G = gen(T + E)
+    w, idx = route_oracle(torch.randn(T, E, generator=G), k)
+    placement = lpt_placement(torch.rand(E, generator=G).tolist(), n_ranks)
+    er = torch.tensor(placement, dtype=torch.int32)
+    el = torch.full((E,), -1, dtype=torch.int32)
+    for d in range(n_ranks):
+        for i, e in enumerate([e for e in range(E) if placement[e] == d]):
+            el[e] = i
+    ref = ep_plan(idx, w, er.long(), el.long(), n_ranks)
+    i32 = dict(dtype=torch.int32, device=DEV)
+    send_token = torch.empty(n_ranks * T, **i32)
+    send_e = torch.empty(n_ranks * T, k, **i32)
+    send_w = torch.empty(n_ranks * T, k, device=DEV)
+    src_pos = torch.empty(T, n_ranks, **i32)
+    count = torch.empty(n_ranks, **i32)
+    err = torch.zeros(1, **i32)
+    st = torch.cuda.current_stream().cuda_stream
+    idx_d, w_d, er_d, el_d = idx.to(DEV), w.to(DEV), er.to(DEV), el.to(DEV)
+    _lib.call("fk_ep_plan", idx_d.data_ptr(), w_d.data_ptr(), T, k, er_d.data_ptr(), el_d.data_ptr(),
+              E, n_ranks, send_token.data_ptr(), send_e.data_ptr(), send_w.data_ptr(),
+              src_pos.data_ptr(), count.data_ptr(), err.data_ptr(), st)
+    assert err.item() == 0
+    for got, want in zip((send_token, send_e, send_w, src_pos, count), ref):
+        assert torch.equal(got.cpu(), want.to(got.dtype)), "plan mismatch"
+    D = 64
+    x = torch.randn(T, D, generator=G).bfloat16().to(DEV)
+    send_x = torch.zeros(n_ranks * T, D, dtype=torch.bfloat16, device=DEV)
+    _lib.call("fk_ep_pack", x.data_ptr(), D, send_token.data_ptr(), n_ranks * T, send_x.data_ptr(),
+              _lib.FK_BF16, st)
+    ok = send_token.long() >= 0
+    assert torch.equal(send_x[ok], x[send_token.long()[ok]])
+    back = torch.randn(n_ranks * T, D, generator=G).bfloat16().to(DEV)
+    out = torch.empty(T, D, dtype=torch.bfloat16, device=DEV)
+    _lib.call("fk_ep_unpack_sum", back.data_ptr(), D, src_pos.data_ptr(), T, n_ranks,
+              out.data_ptr(), _lib.FK_BF16, st)
+    torch.testing.assert_close(out.cpu().double(), ep_unpack_sum(back.cpu(), src_pos.cpu(), T).bfloat16().double(),
+                               atol=1e-2, rtol=1e-2)
+    back_dw = torch.randn(n_ranks * T, k, generator=G).to(DEV)
+    dw = torch.empty(T, k, device=DEV)
+    _lib.call("fk_ep_unpack_dw", back_dw.data_ptr(), idx_d.data_ptr(), er_d.data_ptr(),
+              src_pos.data_ptr(), T, k, n_ranks, E, dw.data_ptr(), st)
+    assert torch.equal(dw.cpu(), ep_unpack_dw(back_dw.cpu(), idx, er.long(), src_pos.cpu()))
+
+
+def _make_weights(D, H, E, seed):
+    G = gen(seed)
+    return (torch.randn(E, D, generator=G) * 0.05, torch.randn(E, H, D, generator=G) * 0.05,
+            torch.randn(E, H, D, generator=G) * 0.05, torch.randn(E, D, H, generator=G) * 0.05)
+
+
+def _single_gpu(D, H, E, k, wts, x, dout):
+    layer = FusedMoEMLPSorted(D, H, E, k)
+    with torch.no_grad():
+        layer.router.weight.copy_(wts[0])
+        for e, ex in enumerate(layer.experts):
+            ex.w_gate.weight.copy_(wts[1][e])
+            ex.w_up.weight.copy_(wts[2][e])
+            ex.w_down.weight.copy_(wts[3][e])
+    layer = layer.to(DEV).bfloat16()
+    xg = x.clone().requires_grad_(True)
+    out = layer(xg)
+    out.backward(dout)
+    return layer, out.detach(), xg.grad
+
+
+def test_ep_layer_one_rank_matches_single_gpu_bitwise():
+    D, H, E, k, T = 256, 256, 16, 4, 512
+    wts = _make_weights(D, H, E, 1)
+    G = gen(2)
+    x = torch.randn(T, D, generator=G).bfloat16().to(DEV)
+    dout = torch.randn(T, D, generator=G).bfloat16().to(DEV)
+    ref_layer, ref_out, ref_dx = _single_gpu(D, H, E, k, wts, x, dout)
+    store = dist.TCPStore("127.0.0.1", _free_port(), 1, True)
+    dist.init_process_group("nccl", store=store, rank=0, world_size=1)
+    try:
+        ep = ExpertParallelMoEMLP(D, H, E, k).to(DEV).bfloat16()
+        ep.load_from_full(*(t.bfloat16().to(DEV) for t in wts))
+        xg = x.clone().requires_grad_(True)
+        out = ep(xg)
+        out.backward(dout)
+        torch.cuda.synchronize()
+        assert torch.equal(out, ref_out)
+        assert torch.equal(xg.grad, ref_dx)
+        assert torch.equal(ep.router.weight.grad, ref_layer.router.weight.grad)
+        for e in range(E):
+            a, b = ep.experts[str(e)], ref_layer.experts[e]
+            assert torch.equal(a.w_gate.weight.grad, b.w_gate.weight.grad)
+            assert torch.equal(a.w_down.weight.grad, b.w_down.weight.grad)
+    finally:
+        dist.destroy_process_group()
+
+
+def _ep_worker(rank, world, port, q):
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    sys.path.insert(0, root)
+    sys.path.insert(0, os.path.join(root, "tests"))
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    try:
+        import datetime
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
+                                world_size=world, timeout=datetime.timedelta(seconds=60))
+        D, H, E, k, T = 256, 256, 16, 4, 256
+        wts = _make_weights(D, H, E, 1)
+        G = torch.Generator().manual_seed(3)
+        x_all = torch.randn(world * T, D, generator=G).bfloat16()
+        d_all = torch.randn(world * T, D, generator=G).bfloat16()
+        ep = ExpertParallelMoEMLP(D, H, E, k, placement=lpt_placement([1.0] * E, world)).to(dev).bfloat16()
+        ep.load_from_full(*(t.bfloat16().to(dev) for t in wts))
+        x = x_all[rank * T:(rank + 1) * T].to(dev).requires_grad_(True)
+        out = ep(x)
+        out.backward(d_all[rank * T:(rank + 1) * T].to(dev))
+        torch.cuda.synchronize()
+        q.put((rank, out.float().cpu(), x.grad.float().cpu()))
+    except Exception as exc:
+        q.put((rank, repr(exc), None))
+    finally:
+        if dist.is_initialized():
+            dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_ep_layer_two_ranks_matches_single_gpu():
+    import torch.multiprocessing as mp
+    D, H, E, k, T, world = 256, 256, 16, 4, 256, 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_ep_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = sorted([q.get(timeout=300) for _ in procs], key=lambda r: r[0])
+    for p in procs:
+        p.join(timeout=60)
+    for r in res:
+        assert not isinstance(r[1], str), f"rank {r[0]}: {r[1]}"
+    wts = _make_weights(D, H, E, 1)
+    G = torch.Generator().manual_seed(3)
+    x_all = torch.randn(world * T, D, generator=G).bfloat16().to(DEV)
+    d_all = torch.randn(world * T, D, generator=G).bfloat16().to(DEV)
+    _, ref_out, ref_dx = _single_gpu(D, H, E, k, wts, x_all, d_all)
+    out = torch.cat([r[1] for r in res])
+    dx = torch.cat([r[2] for r in res])
+    scale = ref_out.abs().max().item()
+    assert (out - ref_out.float().cpu()).abs().max().item() <= 2e-2 * scale
+    scale = ref_dx.abs().max().item()
+    assert (dx - ref_dx.float().cpu()).abs().max().item() <= 2e-2 * scale
