@@ -3,12 +3,11 @@
 // HBM traffic is one read of the logits and one write of the gradient.  A row of V
 // logits (250.5 KiB for V=128256 bf16) is larger than one SM's shared memory; one
 // persistent CTA of 1024 threads per SM owns a row and sweeps it twice: the first sweep
-// streams the row through a ring of shared-memory chunks filled by cp.async.bulk and
-// reduces it to (max, sum exp, sum x) with an online rescale; the second re-reads it from
-// L2 (the chunks were copied with an evict-last policy) and writes the gradient.  The
-// ring runs ahead across rows, so the next row's HBM read overlaps the second sweep.
-// Exponentials of 16-bit inputs are single ex2 instructions with log2(e) folded into an
-// FMA.
+// reduces it to (max, sum exp, sum x) with an online rescale, the second re-reads it from
+// L2 (one row per SM in flight: ~37 MB) and writes the gradient.  Packets move through a
+// per-thread cp.async ring in shared memory, so every thread keeps 8 x 16 bytes in
+// flight.  Exponentials of 16-bit inputs are single ex2 instructions with log2(e) folded
+// into an FMA.
 //
 // The mean-reduction scale 1/n_valid is folded into the gradient write (n_valid comes
 // from a one-CTA prologue that counts non-ignored targets), and the scalar loss is a
@@ -178,12 +177,13 @@ __device__ __forceinline__ Online warp_combine(Online o) {
 }
 
 // Two-sweep row kernel: one CTA of 1024 threads per SM, persistent over rows.
-// Sweep 1 consumes the row from a ring of kRingStages shared-memory chunks filled by
-// cp.async.bulk (thread 0 keeps the ring full, running ahead across row boundaries, so
-// the next row's HBM read overlaps this row's second sweep) and keeps online
-// (max, sum exp, sum x) per thread.  Sweep 2 re-reads the row from L2 -- the chunks were
-// copied with an evict-last policy moments earlier -- and writes the gradient with
-// evict-first stores, so HBM sees one read and one write per element.
+// Sweep 1 reads the row (HBM) and keeps online (max, sum exp, sum x) per thread; sweep 2
+// re-reads it -- it is still in L2: one row per SM is in flight, ~37 MB over the GPU --
+// and writes the gradient with evict-first stores, so HBM sees one read and one write per
+// element.  Both sweeps move packets with cp.async into a per-thread ring of kDepth
+// 16-byte slots in shared memory (each thread reads back only the slots it filled, so no
+// barrier is involved): kDepth packets per thread are in flight without holding
+// registers, 128 KB per SM.
 __device__ __forceinline__ uint64_t policy_evict_last() {
   uint64_t p;
   asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
@@ -194,31 +194,55 @@ __device__ __forceinline__ uint64_t policy_evict_first() {
   asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
   return p;
 }
-__device__ __forceinline__ uint4 ld_hint(const void* ptr, uint64_t pol) {
-  uint4 v;
-  asm volatile("ld.global.L1::no_allocate.L2::cache_hint.v4.u32 {%0, %1, %2, %3}, [%4], %5;"
-               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-               : "l"(ptr), "l"(pol));
-  return v;
-}
 __device__ __forceinline__ void st_hint(void* ptr, uint4 v, uint64_t pol) {
   asm volatile("st.global.L1::no_allocate.L2::cache_hint.v4.u32 [%0], {%1, %2, %3, %4}, %5;" ::"l"(ptr),
                "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w), "l"(pol)
                : "memory");
 }
-__device__ __forceinline__ void bulk_g2s_hint(void* dst, const void* src, uint32_t bytes,
-                                              uint64_t* bar, uint64_t pol) {
-  asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
-      " [%0], [%1], %2, [%3], %4;" ::"r"(ptx::smem_u32(dst)),
-      "l"(src), "r"(bytes), "r"(ptx::smem_u32(bar)), "l"(pol)
-      : "memory");
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, uint64_t pol) {
+  asm volatile("cp.async.cg.shared.global.L2::cache_hint [%0], [%1], 16, %2;" ::"r"(dst), "l"(src),
+               "l"(pol)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
 constexpr int kRowThreads = 1024;
-constexpr int kRowUnroll = 4;
-constexpr int kRingStages = 6;
-constexpr int kChunkPackets = 2048;  // 32 KB per stage: two 16-byte packets per thread
+constexpr int kDepth = 8;  // packets in flight per thread
+
+// Streams the packets v = tid, tid + 1024, ... < nvec of one row through the cp.async
+// ring and calls fn(v, packet) for each, in order.
+template <typename T, typename Fn>
+__device__ __forceinline__ void stream_row(const T* src, int nvec, uint64_t pol, uint32_t ring,
+                                           Fn&& fn) {
+  constexpr int VN = 16 / sizeof(T);
+  const int tid = threadIdx.x;
+  const int n_mine = nvec > tid ? (nvec - 1 - tid) / kRowThreads + 1 : 0;
+#pragma unroll
+  for (int i = 0; i < kDepth; ++i) {
+    if (i < n_mine)
+      cp_async16(ring + (uint32_t)(i * kRowThreads) * 16u, src + (int64_t)(tid + i * kRowThreads) * VN, pol);
+    cp_async_commit();
+  }
+  for (int i = 0; i < n_mine; ++i) {
+    cp_async_wait<kDepth - 1>();
+    const uint32_t slot = ring + (uint32_t)((i % kDepth) * kRowThreads) * 16u;
+    Vec16<T> p;
+    asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(p.u.x), "=r"(p.u.y), "=r"(p.u.z), "=r"(p.u.w)
+                 : "r"(slot));
+    fn(tid + i * kRowThreads, p);
+    const int nx = i + kDepth;
+    if (nx < n_mine) cp_async16(slot, src + (int64_t)(tid + nx * kRowThreads) * VN, pol);
+    cp_async_commit();
+  }
+  cp_async_wait<0>();
+}
 
 template <typename T>
 __global__ void __launch_bounds__(kRowThreads, 1) ce_row_kernel(
@@ -227,75 +251,21 @@ __global__ void __launch_bounds__(kRowThreads, 1) ce_row_kernel(
     float lsm, const int* __restrict__ n_valid_p, float* __restrict__ loss_rows,
     int* __restrict__ err) {
   constexpr int VN = 16 / sizeof(T);
-  extern __shared__ __align__(128) unsigned char ring[];
-  __shared__ __align__(8) uint64_t full[kRingStages], empty[kRingStages];
+  extern __shared__ __align__(128) unsigned char ring_raw[];
   __shared__ float wred[3][32];
   __shared__ float stats[1];
-  __shared__ int dead;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const uint32_t ring = ptx::smem_u32(ring_raw) + (uint32_t)tid * 16u;
   const int nvec = n_cols / VN;
-  const int nchunk = (nvec + kChunkPackets - 1) / kChunkPackets;
   const uint64_t keep = policy_evict_last(), drop = policy_evict_first();
   const float inv_nv = 1.0f / (float)(*n_valid_p);
   const float smooth = lsm / (float)n_cols;
   const float sub = smooth * inv_nv, hsub = (1.0f - lsm) * inv_nv;
-  const int64_t G = gridDim.x;
-  const int64_t my_rows = blockIdx.x < n_rows ? (n_rows - 1 - blockIdx.x) / G + 1 : 0;
-  const int64_t total_chunks = my_rows * nchunk;
-
-  // Producer state (thread 0): next chunk to issue.
-  int64_t q_issue = 0;
-  auto issue = [&](int64_t q) {
-    const int64_t row = blockIdx.x + (q / nchunk) * G;
-    const int c = (int)(q % nchunk);
-    const int s = (int)(q % kRingStages);
-    const int pk = (nvec - c * kChunkPackets) < kChunkPackets ? nvec - c * kChunkPackets : kChunkPackets;
-    const uint32_t bytes = (uint32_t)pk * 16u;
-    ptx::mbar_arrive_expect_tx(&full[s], bytes);
-    bulk_g2s_hint(ring + (size_t)s * kChunkPackets * 16,
-                  logits + row * lstride + (int64_t)c * kChunkPackets * VN, bytes, &full[s], keep);
-  };
-  if (tid == 0) {
-    for (int s = 0; s < kRingStages; ++s) {
-      ptx::mbar_init(&full[s], 1);
-      ptx::mbar_init(&empty[s], kRowThreads / 32);
-    }
-    ptx::fence_mbar_init();
-    dead = 0;
-  }
-  __syncthreads();
-  if (tid == 0)
-    for (; q_issue < total_chunks && q_issue < kRingStages; ++q_issue) issue(q_issue);
-
-  int64_t q = 0;  // consumer chunk counter
-  for (int64_t row = blockIdx.x; row < n_rows; row += G) {
+  for (int64_t row = blockIdx.x; row < n_rows; row += gridDim.x) {
     const T* src = logits + row * lstride;
     const int64_t t = targets[row];
     Online o{-INFINITY, 0.f, 0.f};
-    bool ok = true;
-    for (int c = 0; c < nchunk; ++c, ++q) {
-      const int s = (int)(q % kRingStages);
-      if (!dead && !ptx::mbar_wait(&full[s], (uint32_t)((q / kRingStages) & 1))) ok = false;
-      const int pk = (nvec - c * kChunkPackets) < kChunkPackets ? nvec - c * kChunkPackets : kChunkPackets;
-      const uint4* sv = reinterpret_cast<const uint4*>(ring + (size_t)s * kChunkPackets * 16);
-#pragma unroll
-      for (int u = 0; u < kChunkPackets / kRowThreads; ++u) {
-        const int v = tid + u * kRowThreads;
-        if (v < pk) {
-          Vec16<T> p;
-          p.u = sv[v];
-          online_add_packet<T>(o, p);
-        }
-      }
-      __syncwarp();
-      if (lane == 0) ptx::mbar_arrive(&empty[s]);
-      if (tid == 0) {
-        // Refill this stage once every warp has released it.
-        if (!dead && !ptx::mbar_wait(&empty[s], (uint32_t)((q / kRingStages) & 1))) ok = false;
-        if (!ok) dead = 1;
-        if (!dead && q_issue < total_chunks) issue(q_issue++);
-      }
-    }
+    stream_row<T>(src, nvec, keep, ring, [&](int, const Vec16<T>& p) { online_add_packet<T>(o, p); });
     for (int i = nvec * VN + tid; i < n_cols; i += kRowThreads) online_add_scalar<T>(o, Elt<T>::to_f(src[i]));
     o = warp_combine<T>(o);
     if (lane == 0) {
@@ -306,7 +276,6 @@ __global__ void __launch_bounds__(kRowThreads, 1) ce_row_kernel(
     __syncthreads();
     const bool ignored = (t == ignore_index);
     const bool invalid = !ignored && (t < 0 || t >= n_cols);
-    const bool poisoned = dead != 0;
     if (warp == 0) {
       Online cc{wred[0][lane], wred[1][lane], wred[2][lane]};
       cc = warp_combine<T>(cc);
@@ -316,17 +285,18 @@ __global__ void __launch_bounds__(kRowThreads, 1) ce_row_kernel(
         float loss = invalid ? 0.f : lse - Elt<T>::to_f(src[ignored ? 0 : t]);
         if (lsm > 0.f) loss = (1.0f - lsm) * loss + lsm * (lse - cc.sx / (float)n_cols);
         if (ignored) loss = 0.f;
-        if (invalid || poisoned) loss = __int_as_float(0x7fc00000);
-        if (invalid) atomicExch(err, 1);
-        if (poisoned) atomicExch(err, 2);
+        if (invalid) {
+          loss = __int_as_float(0x7fc00000);
+          atomicExch(err, 1);
+        }
         loss_rows[row] = loss;
       }
     }
     __syncthreads();
     const float lse = stats[0];
     T* dst = grad + row * gstride;
-    if (ignored || invalid || poisoned) {
-      const T z = Elt<T>::from_f((invalid || poisoned) ? __int_as_float(0x7fc00000) : 0.f);
+    if (ignored || invalid) {
+      const T z = Elt<T>::from_f(invalid ? __int_as_float(0x7fc00000) : 0.f);
       Vec16<T> zz;
 #pragma unroll
       for (int e = 0; e < VN; ++e) zz.e[e] = z;
@@ -338,30 +308,21 @@ __global__ void __launch_bounds__(kRowThreads, 1) ce_row_kernel(
         if constexpr (sizeof(T) == 4) return expf(x - lse) * inv_nv - sub;
         else return ex2f(fmaf(x, kLog2e, -cexp)) - sub;
       };
-      const int tv = (int)(t / VN);
-      auto emit = [&](int vv, const Vec16<T>& p) {
+      const int tv = (t < (int64_t)nvec * VN) ? (int)(t / VN) : -1;
+      stream_row<T>(src, nvec, drop, ring, [&](int vv, const Vec16<T>& p) {
         float g[VN];
 #pragma unroll
         for (int e = 0; e < VN; ++e) g[e] = gval(Elt<T>::to_f(p.e[e]));
-        if (vv == tv && t < (int64_t)nvec * VN) g[t - (int64_t)vv * VN] -= hsub;
+        if (vv == tv) {
+          const int te = (int)(t - (int64_t)vv * VN);
+#pragma unroll
+          for (int e = 0; e < VN; ++e) g[e] -= (e == te) ? hsub : 0.f;
+        }
         Vec16<T> o2;
 #pragma unroll
         for (int e = 0; e < VN; ++e) o2.e[e] = Elt<T>::from_f(g[e]);
         st_hint(dst + (int64_t)vv * VN, o2.u, drop);
-      };
-      int w = tid;
-      for (; w + (kRowUnroll - 1) * kRowThreads < nvec; w += kRowUnroll * kRowThreads) {
-        Vec16<T> p[kRowUnroll];
-#pragma unroll
-        for (int u = 0; u < kRowUnroll; ++u) p[u].u = ld_hint(src + (int64_t)(w + u * kRowThreads) * VN, drop);
-#pragma unroll
-        for (int u = 0; u < kRowUnroll; ++u) emit(w + u * kRowThreads, p[u]);
-      }
-      for (; w < nvec; w += kRowThreads) {
-        Vec16<T> p;
-        p.u = ld_hint(src + (int64_t)w * VN, drop);
-        emit(w, p);
-      }
+      });
       for (int i = nvec * VN + tid; i < n_cols; i += kRowThreads) {
         float g = gval(Elt<T>::to_f(src[i]));
         if ((int64_t)i == t) g -= hsub;
@@ -463,7 +424,7 @@ int fwd_t(const void* logits, int64_t ls, void* grad, int64_t gs, const int64_t*
                        ((gs * (int64_t)sizeof(T)) % 16 == 0);
     if (rowvec) {
       int64_t g = n_rows < (int64_t)num_sms() ? n_rows : (int64_t)num_sms();
-      const int smem = kRingStages * kChunkPackets * 16;
+      const int smem = kDepth * kRowThreads * 16;
       cudaFuncSetAttribute(ce_row_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
       ce_row_kernel<T><<<(int)g, kRowThreads, smem, st>>>(lp, ls, gp, gs, targets, n_rows,
                                                           (int)n_cols, ignore, lsm, n_valid,
