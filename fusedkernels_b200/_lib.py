@@ -28,6 +28,7 @@ SIGNATURES: dict[str, list] = {
     "fk_rmsnorm_fwd": [_vp, _i64, _vp, _i32, _vp, _i64, _vp, _i64, _i64, _f32, _i32, _vp],
     "fk_rmsnorm_bwd_workspace_size": [_i64, _i64, C.POINTER(_sz)],
     "fk_rmsnorm_bwd": [_vp, _vp, _vp, _i32, _vp, _vp, _vp, _vp, _sz, _i64, _i64, _i32, _vp],
+    "fk_rmsnorm_bwd_noalloc": [_vp, _vp, _vp, _i32, _vp, _vp, _vp, _i64, _i64, _i32, _vp],
     "fk_router_fwd": [_vp, _i64, _i32, _i64, _i32, _i32, _vp, _vp, _vp],
     "fk_router_bwd": [_vp, _vp, _vp, _vp, _i64, _i32, _i32, _vp],
     "fk_ce_fwd": [_vp, _i64, _vp, _i64, _vp, _i64, _i64, _i64, _f32, _i32, _vp, _vp, _vp, _vp,

@@ -17,6 +17,7 @@
 // Generic path: any cols / alignment, scalar element loops re-reading the row.
 #include "common.cuh"
 #include "ptx.cuh"
+#include <mutex>
 
 namespace fk {
 namespace {
@@ -668,5 +669,123 @@ extern "C" int fk_rmsnorm_bwd(const void* dy, const void* x, const void* weight,
                                                       dy, x, weight, rstd, dx, dw,
                                                       static_cast<float*>(workspace), rows, cols,
                                                       fk::as_stream(stream))));
+  return FK_OK;
+}
+
+// ------------------------------------------------------------------ fixed-scratch variant
+// fk_rmsnorm_bwd_noalloc: the same backward for callers that cannot allocate device memory
+// -- code that only receives the tensors of another framework's memory pool, runs under a
+// pre-planned memory budget, or executes where allocation calls are not allowed -- and so
+// cannot hand fk_rmsnorm_bwd its workspace.  The per-CTA weight-gradient partials live in
+// a fixed file-scope device array instead (kNoAllocScratchBytes, held by every GPU that
+// loads the library until the process exits).
+namespace fk {
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = size_t(8) << 20;  // 8 MiB per device
+constexpr int64_t kNoAllocScratchFloats = (int64_t)(kNoAllocScratchBytes / sizeof(float));
+static __device__ __align__(256) float g_rmsnorm_scratch[kNoAllocScratchFloats];
+
+// Device address of g_rmsnorm_scratch for the current device, looked up once per device
+// (host code cannot use the symbol itself: on the host it names a stand-in object).
+int scratch_address(float** out) {
+  static std::mutex mu;
+  static float* addr[64] = {nullptr};
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess || dev < 0 || dev >= 64)
+    return fail(FK_ERR_NO_DEVICE, "fk_rmsnorm_bwd_noalloc: no current device (%s)",
+                cudaGetErrorString(e));
+  std::lock_guard<std::mutex> lock(mu);
+  if (addr[dev] == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_rmsnorm_scratch);
+    if (e != cudaSuccess || p == nullptr)
+      return fail(FK_ERR_NO_DEVICE, "fk_rmsnorm_bwd_noalloc: cudaGetSymbolAddress failed (%s)",
+                  cudaGetErrorString(e));
+    addr[dev] = static_cast<float*>(p);
+  }
+  *out = addr[dev];
+  return FK_OK;
+}
+
+// Same kernels and launch plan as bwd_t, with the grid (= number of partial rows) capped
+// so the partials fit the fixed scratch.
+template <typename T, typename W>
+int bwd_noalloc_t(const void* dy, const void* x, const void* w, const float* rstd, void* dx,
+                  void* dw, float* part, int64_t max_grid, int64_t rows, int64_t cols,
+                  cudaStream_t s) {
+  const bool al = aligned16(dy) && aligned16(x) && aligned16(dx);
+  Plan p = plan_rows(cols, sizeof(T), al, true);
+  const T* dyp = static_cast<const T*>(dy);
+  const T* xp = static_cast<const T*>(x);
+  T* dxp = static_cast<T*>(dx);
+  auto cap = [&](int g) { return (int)((int64_t)g < max_grid ? g : max_grid); };
+  int grid = 1;
+  const int rv = ring_vpt(cols, sizeof(T), al);
+  if (rv > 0) {
+    const int smem = kRingStages * 2 * (int)(cols * sizeof(T));
+    switch (rv) {
+#define FK_CASE(V)                                                                      \
+  case V: {                                                                             \
+    auto k = rmsnorm_bwd_ring<T, W, V>;                                                 \
+    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);          \
+    grid = cap(persistent_grid(k, kRingThreads, rows, smem));                           \
+    k<<<grid, kRingThreads, smem, s>>>(dyp, xp, w, rstd, dxp, part, rows, (int)cols);     \
+    break;                                                                              \
+  }
+      FK_CASE(1) FK_CASE(2) FK_CASE(4)
+#undef FK_CASE
+    }
+  } else if (p.reg) {
+    switch (p.vpt) {
+#define FK_CASE(V)                                                                      \
+  case V: {                                                                             \
+    auto k = rmsnorm_bwd_reg<T, W, V, (V == 1 ? 3 : 2)>;                                \
+    grid = cap(persistent_grid(k, p.threads, rows));                                    \
+    k<<<grid, p.threads, 0, s>>>(dyp, xp, w, rstd, dxp, part, rows, (int)cols);         \
+    break;                                                                              \
+  }
+      FK_CASE(1) FK_CASE(2)
+#undef FK_CASE
+    }
+  } else {
+    auto k = rmsnorm_bwd_generic<T, W>;
+    grid = cap(persistent_grid(k, 256, rows));
+    k<<<grid, 256, 0, s>>>(dyp, xp, w, rstd, dxp, part, rows, cols);
+  }
+  int st = launch_status("fk_rmsnorm_bwd_noalloc");
+  if (st != FK_OK) return st;
+  const int rgrid = (int)((cols + 31) / 32);
+  rmsnorm_dw_reduce<W><<<rgrid, 1024, 0, s>>>(part, grid, cols, static_cast<W*>(dw));
+  return launch_status("fk_rmsnorm_bwd_noalloc(dw reduce)");
+}
+
+}  // namespace
+}  // namespace fk
+
+extern "C" int fk_rmsnorm_bwd_noalloc(const void* dy, const void* x, const void* weight,
+                                      int w_dtype, const float* rstd, void* dx, void* dw,
+                                      int64_t rows, int64_t cols, int dtype, void* stream) {
+  FK_CHECK_ARG(rows >= 0 && cols >= 0, "fk_rmsnorm_bwd_noalloc: negative shape");
+  if (cols == 0) return FK_OK;
+  FK_CHECK_ARG(dw && weight, "fk_rmsnorm_bwd_noalloc: null pointer");
+  if (cols > fk::kNoAllocScratchFloats)
+    return fk::fail(FK_ERR_UNSUPPORTED,
+                    "fk_rmsnorm_bwd_noalloc: cols=%lld exceeds the fixed scratch (at most %lld "
+                    "columns: one fp32 partial row of 8 MiB); use fk_rmsnorm_bwd with a workspace",
+                    (long long)cols, (long long)fk::kNoAllocScratchFloats);
+  if (rows == 0) {
+    cudaMemsetAsync(dw, 0, (size_t)cols * fk::dtype_size(w_dtype), fk::as_stream(stream));
+    return fk::launch_status("fk_rmsnorm_bwd_noalloc(zero dw)");
+  }
+  FK_CHECK_ARG(dy && x && rstd && dx, "fk_rmsnorm_bwd_noalloc: null pointer");
+  float* part = nullptr;
+  int st = fk::scratch_address(&part);
+  if (st != FK_OK) return st;
+  const int64_t max_grid = fk::kNoAllocScratchFloats / cols;  // partial rows that fit
+  FK_DISPATCH_DTYPE(dtype, FK_DISPATCH_W(w_dtype, return fk::bwd_noalloc_t<scalar_t, wt>(
+                                                      dy, x, weight, rstd, dx, dw, part, max_grid,
+                                                      rows, cols, fk::as_stream(stream))));
   return FK_OK;
 }

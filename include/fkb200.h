@@ -79,6 +79,23 @@ FK_API int fk_rmsnorm_bwd(const void* dy, const void* x, const void* weight, int
                    size_t workspace_bytes, int64_t rows, int64_t cols, int dtype,
                    void* stream);
 
+/* No counterpart in the reference.  Backward of RMSNorm for callers that cannot allocate
+ * device memory (for example code that only receives tensors from another framework's
+ * memory pool, or that must run inside a fixed, pre-planned memory budget) and therefore
+ * cannot pass fk_rmsnorm_bwd its workspace.  Results equal fk_rmsnorm_bwd's (dx exactly;
+ * dw up to fp32 summation order when the shape needs more partial rows than fit).
+ * The weight-gradient partials go to one fixed 8 MiB device array inside the library, which
+ * every GPU that loads the library keeps until the process exits; cols must be at most
+ * 2,097,152 (one fp32 partial row), larger cols are rejected with FK_ERR_UNSUPPORTED.
+ * The first call on a device looks the array's device address up (cudaGetSymbolAddress);
+ * make that first call before any CUDA stream capture.  Every call uses the same array:
+ * calls that may run at the same time on the GPU (different streams, or different host
+ * threads on one device) race on it and must be serialised by the caller.
+ * Allocates nothing: no cudaMalloc/cudaFree and no allocating library call. */
+FK_API int fk_rmsnorm_bwd_noalloc(const void* dy, const void* x, const void* weight, int w_dtype,
+                                  const float* rstd, void* dx, void* dw, int64_t rows,
+                                  int64_t cols, int dtype, void* stream);
+
 /* ---------------------------------------------------------------- MoE router -----
  * Per row of logits [n_rows, n_experts] (row stride in elements): rank experts by the
  * exact logit value (ties -> lower expert index first; -0.0 == +0.0; NaN ranks above
