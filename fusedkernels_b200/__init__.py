@@ -7,11 +7,15 @@ C ABI in include/fkb200.h.  There is no CPU or Triton fallback.
 from .cross_entropy import fused_cross_entropy
 from .rmsnorm import FusedRMSNorm
 from .swiglu import fused_swiglu
+from .moe_routing import fused_moe_route
 from .moe_routing_v2 import fused_moe_route_v2
+from .moe_routing_v4 import fused_moe_route_v4
+from .moe_layer import FusedMoEMLP
 from .moe_layer_sorted import FusedMoEMLPSorted
 
 __all__ = [
-    "fused_cross_entropy", "FusedRMSNorm", "fused_swiglu", "fused_moe_route_v2",
-    "FusedMoEMLPSorted",
+    "fused_cross_entropy", "FusedRMSNorm", "fused_swiglu",
+    "fused_moe_route", "fused_moe_route_v2", "fused_moe_route_v4",
+    "FusedMoEMLP", "FusedMoEMLPSorted",
 ]
 __version__ = "0.2.0+b200"

@@ -22,3 +22,17 @@ class Expert(nn.Module):
 
     def forward(self, x):
         return self.w_down(F.silu(self.w_gate(x)) * self.w_up(x))
+
+
+
+# Imported after Expert is defined: moe_layer_sorted imports Expert from this module.
+from .moe_layer_sorted import FusedMoEMLPSorted  # noqa: E402
+
+
+class FusedMoEMLP(FusedMoEMLPSorted):
+    """Masked-dispatch MoE layer API (fusedkernels/moe_layer.py:34-64).
+
+    The reference loops over experts with boolean masks; its output is the same function
+    of the inputs as the sorted-dispatch layer (out[t] = sum_j w[t,j] Expert_{idx[t,j]}(x[t])),
+    so this class keeps the constructor, submodules and state_dict keys and runs the
+    sorted-dispatch tensor-core path."""

@@ -26,6 +26,7 @@ import torch.nn as nn
 
 from . import _lib
 from .moe_layer import Expert
+from .moe_routing import fused_moe_route
 from .moe_routing_v2 import fused_moe_route_v2
 
 
@@ -213,10 +214,9 @@ class FusedMoEMLPSorted(nn.Module):
         if x_flat.dtype != torch.bfloat16 or self.w13.dtype != torch.bfloat16:
             raise TypeError("FusedMoEMLPSorted runs on bf16 tensor cores: use bfloat16 "
                             "activations and call .bfloat16() on the layer")
-        if self.router_version != "v2":
-            raise NotImplementedError("router_version='v1' is not on the B200 fused path")
         x_flat = x_flat.contiguous()
         router_logits = self.router(x_flat)
-        topk_weights, topk_idx = fused_moe_route_v2(router_logits, self.k)
+        route_fn = fused_moe_route_v2 if self.router_version == "v2" else fused_moe_route
+        topk_weights, topk_idx = route_fn(router_logits, self.k)
         out = _SortedMoEFn.apply(x_flat, topk_weights, topk_idx, self, *self._expert_params())
         return out.reshape(orig_shape)

@@ -20,3 +20,24 @@ def test_ops_require_cuda_tensors():
 def test_public_names():
     for name in ["fused_cross_entropy", "FusedRMSNorm", "fused_swiglu", "fused_moe_route_v2"]:
         assert hasattr(fk, name)
+
+
+def test_full_public_api_names():
+    """fusedkernels/__init__.py:10-14 exports."""
+    for name in ["fused_cross_entropy", "FusedRMSNorm", "fused_swiglu", "fused_moe_route",
+                 "fused_moe_route_v2", "fused_moe_route_v4", "FusedMoEMLP", "FusedMoEMLPSorted"]:
+        assert name in fk.__all__ and hasattr(fk, name)
+
+
+def test_moe_layers_keep_reference_parameters():
+    m = fk.FusedMoEMLPSorted(64, 128, 4, 2)
+    keys = list(m.state_dict().keys())
+    assert keys == ["router.weight"] + [f"experts.{e}.{n}.weight" for e in range(4)
+                                        for n in ("w_gate", "w_up", "w_down")]
+    assert m.experts[1].w_up.weight.data_ptr() == m.w13[1, 128:].data_ptr()
+    masked = fk.FusedMoEMLP(64, 128, 4, 2, router_version="v1")
+    assert isinstance(masked, fk.FusedMoEMLPSorted) and masked.router_version == "v1"
+    sd = m.state_dict()
+    masked.load_state_dict(sd)
+    assert masked.w13.data_ptr() == masked.experts[0].w_gate.weight.data_ptr()
+    assert all(p.is_leaf for p in masked.parameters())

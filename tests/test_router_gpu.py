@@ -126,3 +126,46 @@ def test_router_deterministic():
     outs = [run(logits, 32, torch.ones(1024, 32)) for _ in range(5)]
     for o in outs[1:]:
         assert all(torch.equal(a, b) for a, b in zip(o, outs[0]))
+
+
+# ------------------------------------------------------------------ v1 / v4 router APIs
+@pytest.mark.parametrize("E,k", [(8, 2), (16, 4), (64, 8), (128, 1)])
+def test_v1_api_matches_oracle(E, k):
+    """tests/test_moe_correctness.py:18-49 cases, exact ordered indices."""
+    logits = torch.randn(1024, E, generator=gen(E + k))
+    lg = logits.cuda().requires_grad_(True)
+    w, idx = fk.fused_moe_route(lg, k)
+    rw, ridx = route_oracle(logits, k)
+    assert torch.equal(idx.cpu(), ridx)
+    torch.testing.assert_close(w.detach().cpu(), rw, atol=1e-6, rtol=1e-5)
+    w.sum().backward()
+    assert lg.grad.shape == logits.shape
+
+
+@pytest.mark.parametrize("E,k", [(8, 2), (16, 4), (16, 8), (32, 4), (32, 8), (32, 16), (64, 8),
+                                 (64, 16), (64, 32), (128, 8), (128, 16), (128, 32), (32, 3),
+                                 (64, 5), (128, 7), (64, 11)])
+def test_v4_api_ascending_order_and_grad(E, k):
+    """tests/test_moe_routing_v4.py:22-94 cases: v4 returns the top k in ascending order."""
+    import warnings
+    logits = torch.randn(1024, E, generator=gen(100 + E + k))
+    dw = torch.randn(1024, k, generator=gen(7))
+    lg = logits.cuda().requires_grad_(True)
+    with warnings.catch_warnings():
+        warnings.simplefilter("ignore")
+        w, idx = fk.fused_moe_route_v4(lg, k)
+    rw, ridx = route_oracle(logits, k)
+    assert torch.equal(idx.cpu(), ridx.flip(-1))
+    torch.testing.assert_close(w.detach().cpu(), rw.flip(-1), atol=1e-6, rtol=1e-5)
+    w.backward(dw.cuda())
+    torch.testing.assert_close(lg.grad.cpu(), route_bwd_oracle(logits, k, dw.flip(-1)),
+                               atol=1e-5, rtol=1e-4)
+
+
+def test_v4_warns_for_large_k_and_is_deterministic():
+    logits = torch.randn(1024, 128, generator=gen(4)).cuda()
+    with pytest.warns(UserWarning):
+        _, first = fk.fused_moe_route_v4(logits, 80)
+    for _ in range(4):
+        _, again = fk.fused_moe_route_v4(logits, 32)
+        assert torch.equal(again, fk.fused_moe_route_v4(logits, 32)[1])
