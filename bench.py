@@ -820,7 +820,13 @@ def run_ours(args):
                           else f"{reps} eager steps through the public API, CUDA events"),
                "clocks": clk.summary()}
         print(json.dumps(out), flush=True)
+    # Graphs that hold NCCL calls must be released before the process group.
+    graph = run_step = None
+    torch.cuda.synchronize(dev)
+    import gc
+    gc.collect()
     if torch.distributed.is_initialized():
+        torch.distributed.barrier()
         torch.distributed.destroy_process_group()
 
 
