@@ -128,7 +128,7 @@ __device__ __forceinline__ Online combine(Online a, Online b) {
   return r;
 }
 
-template <typename T, bool SX = true>
+template <typename T>
 __device__ __forceinline__ void online_add_packet(Online& o, const Vec16<T>& p) {
   constexpr int VN = Vec16<T>::N;
   float x[VN];
@@ -137,20 +137,17 @@ __device__ __forceinline__ void online_add_packet(Online& o, const Vec16<T>& p) 
   for (int e = 0; e < VN; ++e) {
     x[e] = Elt<T>::to_f(p.e[e]);
     pm = fmaxf(pm, x[e]);
-    if (SX) o.sx += x[e];
+    o.sx += x[e];
   }
-  if (pm > o.m) {  // new running max (rare after the first packets)
-    o.s = (o.m == -INFINITY) ? 0.f : o.s * exp_shift<T>(o.m, pm);
-    o.m = pm;
+  const float mn = fmaxf(o.m, pm);
+  if (mn == -INFINITY) return;
+  if (o.m != mn) {
+    o.s = (o.m == -INFINITY) ? 0.f : o.s * exp_shift<T>(o.m, mn);
+    o.m = mn;
   }
-  if (o.m == -INFINITY) return;
-  const float mb = o.m * kLog2e;
   float acc = 0.f;
 #pragma unroll
-  for (int e = 0; e < VN; ++e) {
-    if constexpr (sizeof(T) == 4) acc += expf(x[e] - o.m);
-    else acc += ex2f(fmaf(x[e], kLog2e, -mb));
-  }
+  for (int e = 0; e < VN; ++e) acc += exp_shift<T>(x[e], mn);
   o.s += acc;
 }
 
@@ -224,31 +221,24 @@ template <typename T, typename Fn>
 __device__ __forceinline__ void stream_row(const T* src, int nvec, uint64_t pol, uint32_t ring,
                                            Fn&& fn) {
   constexpr int VN = 16 / sizeof(T);
-  constexpr int64_t kStep = (int64_t)kRowThreads * VN;  // elements between a thread's packets
   const int tid = threadIdx.x;
   const int n_mine = nvec > tid ? (nvec - 1 - tid) / kRowThreads + 1 : 0;
-  const T* next = src + (int64_t)tid * VN;  // next packet to copy
 #pragma unroll
   for (int i = 0; i < kDepth; ++i) {
-    if (i < n_mine) {
-      cp_async16(ring + (uint32_t)(i * kRowThreads) * 16u, next, pol);
-      next += kStep;
-    }
+    if (i < n_mine)
+      cp_async16(ring + (uint32_t)(i * kRowThreads) * 16u, src + (int64_t)(tid + i * kRowThreads) * VN, pol);
     cp_async_commit();
   }
-  int v = tid;
-  for (int i = 0; i < n_mine; ++i, v += kRowThreads) {
+  for (int i = 0; i < n_mine; ++i) {
     cp_async_wait<kDepth - 1>();
-    const uint32_t slot = ring + (uint32_t)((i & (kDepth - 1)) * kRowThreads) * 16u;
+    const uint32_t slot = ring + (uint32_t)((i % kDepth) * kRowThreads) * 16u;
     Vec16<T> p;
     asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
                  : "=r"(p.u.x), "=r"(p.u.y), "=r"(p.u.z), "=r"(p.u.w)
                  : "r"(slot));
-    fn(v, p);
-    if (i + kDepth < n_mine) {
-      cp_async16(slot, next, pol);
-      next += kStep;
-    }
+    fn(tid + i * kRowThreads, p);
+    const int nx = i + kDepth;
+    if (nx < n_mine) cp_async16(slot, src + (int64_t)(tid + nx * kRowThreads) * VN, pol);
     cp_async_commit();
   }
   cp_async_wait<0>();
@@ -275,10 +265,7 @@ __global__ void __launch_bounds__(kRowThreads, 1) ce_row_kernel(
     const T* src = logits + row * lstride;
     const int64_t t = targets[row];
     Online o{-INFINITY, 0.f, 0.f};
-    if (lsm > 0.f)
-      stream_row<T>(src, nvec, keep, ring, [&](int, const Vec16<T>& p) { online_add_packet<T, true>(o, p); });
-    else
-      stream_row<T>(src, nvec, keep, ring, [&](int, const Vec16<T>& p) { online_add_packet<T, false>(o, p); });
+    stream_row<T>(src, nvec, keep, ring, [&](int, const Vec16<T>& p) { online_add_packet<T>(o, p); });
     for (int i = nvec * VN + tid; i < n_cols; i += kRowThreads) online_add_scalar<T>(o, Elt<T>::to_f(src[i]));
     o = warp_combine<T>(o);
     if (lane == 0) {
