@@ -21,6 +21,8 @@
 // gradients): for expert e the reduction runs over its token segment; A and B are
 // token-major (MN-major operands) and the output is expert e's [M, N] gradient.
 //
+// Epilogue stores go through a per-warp ring of shared-memory chunks and TMA stores
+// (coalesced 64-byte rows instead of per-thread 16-byte row fragments).
 // Epilogues: plain bf16 store; SwiGLU forward (the B tile holds BN/2 gate rows and the
 // matching BN/2 up rows, so the tile yields h1 = (g, u) and act = silu(g) * u); SwiGLU
 // backward (reads g, u of the tile's hidden units and writes (dg, du)).
@@ -58,6 +60,7 @@ struct Params {
   const __nv_bfloat16* in0;  // SWIGLU_BWD: h1 [rows, 2H]
   int64_t ldi0;
   int* err;
+  int tma_store;  // epilogue writes through shared memory + TMA stores (tmC0 / tmC1)
 };
 
 __device__ __forceinline__ uint64_t globaltimer() {
@@ -175,6 +178,49 @@ __device__ __forceinline__ void load32(const __nv_bfloat16* src, float (&v)[32])
   }
 }
 
+// Epilogue output path: each epilogue warp owns a ring of kRingBufs 2 KB shared-memory
+// buffers; a 32-row x 32-column bf16 chunk is written into one (64-byte rows, 64-byte
+// swizzle, so the 16-byte writes of a warp hit distinct banks) and stored to global memory
+// by one TMA store issued by lane 0.  A buffer is reused only after the bulk store that
+// read it four chunks earlier has finished reading.
+constexpr int kRingBufs = 4;
+constexpr uint32_t kChunkBytes = 32 * 32 * 2;
+constexpr uint32_t kRingBytesPerWarp = kRingBufs * kChunkBytes;
+
+struct StoreRing {
+  uint32_t base;
+  int next;
+  __device__ __forceinline__ void put(const CUtensorMap* map, int col, int row,
+                                      const float (&v)[32], int lane) {
+    if (lane == 0) asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(kRingBufs - 1) : "memory");
+    __syncwarp();
+    const uint32_t buf = base + (uint32_t)next * kChunkBytes;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const uint32_t addr = buf + (uint32_t)lane * 64u + ((uint32_t)(q ^ ((lane >> 1) & 3)) << 4);
+      asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr),
+                   "r"(pack_bf16(v[8 * q], v[8 * q + 1])), "r"(pack_bf16(v[8 * q + 2], v[8 * q + 3])),
+                   "r"(pack_bf16(v[8 * q + 4], v[8 * q + 5])), "r"(pack_bf16(v[8 * q + 6], v[8 * q + 7]))
+                   : "memory");
+    }
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    __syncwarp();
+    if (lane == 0) {
+      asm volatile(
+          "cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
+              reinterpret_cast<uint64_t>(map)),
+          "r"(col), "r"(row), "r"(buf)
+          : "memory");
+      asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+    }
+    next = (next + 1) & (kRingBufs - 1);
+  }
+  __device__ __forceinline__ void drain(int lane) {
+    if (lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+    __syncwarp();
+  }
+};
+
 struct Tile {
   int e, m0, n0, kb0, kiters;
   bool valid;
@@ -219,7 +265,9 @@ __device__ __forceinline__ Tile decode(const Params& p, int t) {
 template <int BN, int STAGES, bool A_MN, bool B_MN, int MODE, int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
     moe_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
-                    const __grid_constant__ CUtensorMap tmB, const Params p) {
+                    const __grid_constant__ CUtensorMap tmB,
+                    const __grid_constant__ CUtensorMap tmC0,
+                    const __grid_constant__ CUtensorMap tmC1, const Params p) {
   constexpr uint32_t A_BYTES = BM * BK * 2;
   constexpr uint32_t B_BYTES = BN * BK * 2;
   constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
@@ -227,7 +275,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem = reinterpret_cast<unsigned char*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+  const uint32_t ring_base = ptx::smem_u32(smem + STAGES * STAGE_BYTES);  // 4 warps x ring
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES + 4 * kRingBytesPerWarp);
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;
@@ -341,6 +390,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // -------------------------------------------------------------- epilogue (128 thr)
     const int q = warp & 3;  // TMEM lane quarter this warp may access
     const int row_in_tile = q * 32 + lane;
+    StoreRing ring{ring_base + (uint32_t)(warp - 2) * kRingBytesPerWarp, 0};
     int it = 0;
     for (int t = blockIdx.x; t < ntiles; t += gridDim.x) {
       const Tile tl = decode<BN, MODE, EPI>(p, t);
@@ -352,6 +402,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const uint32_t tbase = tmem_base + (uint32_t)(acc * BN) + ((uint32_t)(q * 32) << 16);
       const bool zero = tl.kiters == 0;
+      const int row0 = tl.m0 + q * 32;  // first row of this warp's 32-row slab
       if (MODE == MODE_K) {
         // tcgen05.ld is warp-collective: every lane loads, only rows < M store.
         const int m = tl.m0 + row_in_tile;
@@ -365,7 +416,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           } else {
             tmem_ld32(tbase + c, v);
           }
-          if (m < p.M) store32(dst + c, v);
+          if (p.tma_store) ring.put(&tmC0, tl.n0 + c, tl.e * p.M + row0, v, lane);
+          else if (m < p.M) store32(dst + c, v);
         }
       } else {
         const int64_t row = tl.m0 + row_in_tile;
@@ -375,7 +427,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int c = 0; c < BN; c += 32) {
             float v[32];
             tmem_ld32(tbase + c, v);
-            store32(dst + c, v);
+            if (p.tma_store) ring.put(&tmC0, tl.n0 + c, row0, v, lane);
+            else store32(dst + c, v);
           }
         } else if (EPI == EPI_SWIGLU_FWD) {
           __nv_bfloat16* act = p.out0 + row * p.ld0 + tl.n0;
@@ -388,9 +441,15 @@ __global__ void __launch_bounds__(kThreads, 1)
             tmem_ld32(tbase + BN / 2 + c, u);
 #pragma unroll
             for (int i = 0; i < 32; ++i) a[i] = g[i] * sigmoidf_t<__nv_bfloat16>(g[i]) * u[i];
-            store32(hg + c, g);
-            store32(hu + c, u);
-            store32(act + c, a);
+            if (p.tma_store) {
+              ring.put(&tmC1, tl.n0 + c, row0, g, lane);
+              ring.put(&tmC1, p.H + tl.n0 + c, row0, u, lane);
+              ring.put(&tmC0, tl.n0 + c, row0, a, lane);
+            } else {
+              store32(hg + c, g);
+              store32(hu + c, u);
+              store32(act + c, a);
+            }
           }
         } else {  // EPI_SWIGLU_BWD: accumulator = d(act) for hidden units n0 .. n0+BN
           const __nv_bfloat16* hg = p.in0 + row * p.ldi0 + tl.n0;
@@ -409,14 +468,20 @@ __global__ void __launch_bounds__(kThreads, 1)
               ou[i] = d[i] * g[i] * sg;
               og[i] = d[i] * u[i] * (sg * (1.0f + g[i] * (1.0f - sg)));
             }
-            store32(dg + c, og);
-            store32(du + c, ou);
+            if (p.tma_store) {
+              ring.put(&tmC0, tl.n0 + c, row0, og, lane);
+              ring.put(&tmC0, p.H + tl.n0 + c, row0, ou, lane);
+            } else {
+              store32(dg + c, og);
+              store32(du + c, ou);
+            }
           }
         }
       }
       tc_fence_before();
       ptx::mbar_arrive(&tempty[acc]);
     }
+    ring.drain(lane);
   }
   tc_fence_before();
   __syncthreads();
@@ -451,7 +516,8 @@ static EncodeTiledFn encode_fn() {
 // bf16 tensor map, 128-byte swizzle; dims/strides innermost first (strides in bytes,
 // rank-1 entries), box innermost first.
 static int make_map(CUtensorMap* m, const void* base, int rank, const uint64_t* dims,
-                    const uint64_t* strides, const uint32_t* box) {
+                    const uint64_t* strides, const uint32_t* box,
+                    CUtensorMapSwizzle swz = CU_TENSOR_MAP_SWIZZLE_128B) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) return fail(FK_ERR_NO_DEVICE, "cuTensorMapEncodeTiled unavailable");
   cuuint64_t d[3], st[2];
@@ -462,23 +528,31 @@ static int make_map(CUtensorMap* m, const void* base, int rank, const uint64_t* 
   }
   for (int i = 0; i < rank - 1; ++i) st[i] = strides[i];
   CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, rank, const_cast<void*>(base), d, st, b, es,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(FK_ERR_INVALID_ARG, "cuTensorMapEncodeTiled failed (%d)", (int)r);
   return FK_OK;
 }
 
+// Epilogue output map: bf16 [rows, cols] (row stride ld elements), 32 x 32 boxes, 64-byte
+// swizzle (matching the StoreRing layout).
+static int make_out_map(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, int64_t ld) {
+  uint64_t d[2] = {(uint64_t)cols, (uint64_t)rows}, st[1] = {(uint64_t)ld * 2};
+  uint32_t box[2] = {32, 32};
+  return make_map(m, base, 2, d, st, box, CU_TENSOR_MAP_SWIZZLE_64B);
+}
+
 template <int BN, bool A_MN, bool B_MN, int MODE, int EPI>
-static int launch(const CUtensorMap& a, const CUtensorMap& b, const Params& p, int max_tiles,
-                  cudaStream_t st) {
+static int launch(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& c0,
+                  const CUtensorMap& c1, const Params& p, int max_tiles, cudaStream_t st) {
   constexpr int STAGE_BYTES = (BM + BN) * BK * 2;
   constexpr int STAGES = (BN == 256) ? 4 : (BN == 128 ? 6 : 8);
-  constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 256;
+  constexpr int SMEM = STAGES * STAGE_BYTES + 4 * (int)kRingBytesPerWarp + 1024 + 256;
   auto k = moe_gemm_kernel<BN, STAGES, A_MN, B_MN, MODE, EPI>;
   cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
   int grid = num_sms();
   if (max_tiles < grid) grid = max_tiles < 1 ? 1 : max_tiles;
-  k<<<grid, kThreads, SMEM, st>>>(a, b, p);
+  k<<<grid, kThreads, SMEM, st>>>(a, b, c0, c1, p);
   return launch_status("fk_moe_gemm");
 }
 
@@ -543,9 +617,14 @@ extern "C" int fk_moe_gemm_up(const void* xs, int64_t max_rows, int dim, const v
   p.ld1 = 2 * (int64_t)hidden;
   p.err = err_flag;
   const int max_tiles = (int)(max_rows / G::BM) * (hidden / (bn / 2));
+  CUtensorMap mc0, mc1;
+  if ((st = G::make_out_map(&mc0, act, max_rows, hidden, hidden))) return st;
+  if ((st = G::make_out_map(&mc1, h1, max_rows, 2 * hidden, 2 * hidden))) return st;
+  p.tma_store = 1;
   cudaStream_t s = fk::as_stream(stream);
-  if (bn == 256) return G::launch<256, false, false, G::MODE_M, G::EPI_SWIGLU_FWD>(ma, mb, p, max_tiles, s);
-  return G::launch<128, false, false, G::MODE_M, G::EPI_SWIGLU_FWD>(ma, mb, p, max_tiles, s);
+  if (bn == 256)
+    return G::launch<256, false, false, G::MODE_M, G::EPI_SWIGLU_FWD>(ma, mb, mc0, mc1, p, max_tiles, s);
+  return G::launch<128, false, false, G::MODE_M, G::EPI_SWIGLU_FWD>(ma, mb, mc0, mc1, p, max_tiles, s);
 }
 
 extern "C" int fk_moe_gemm_down(const void* act, int64_t max_rows, int hidden, const void* w2,
@@ -577,8 +656,11 @@ extern "C" int fk_moe_gemm_down(const void* act, int64_t max_rows, int hidden, c
   p.ld0 = dim;
   p.err = err_flag;
   const int max_tiles = (int)(max_rows / G::BM) * (dim / bn);
+  CUtensorMap mc0;
+  if ((st = G::make_out_map(&mc0, y, max_rows, dim, dim))) return st;
+  p.tma_store = 1;
   cudaStream_t s = fk::as_stream(stream);
-  FK_BN_SWITCH(bn, return G::launch<BN_, false, false, G::MODE_M, G::EPI_STORE>(ma, mb, p, max_tiles, s));
+  FK_BN_SWITCH(bn, return G::launch<BN_, false, false, G::MODE_M, G::EPI_STORE>(ma, mb, mc0, mc0, p, max_tiles, s));
   return FK_OK;
 }
 
@@ -615,8 +697,11 @@ extern "C" int fk_moe_gemm_down_dgrad(const void* dy, int64_t max_rows, int dim,
   p.ldi0 = 2 * (int64_t)hidden;
   p.err = err_flag;
   const int max_tiles = (int)(max_rows / G::BM) * (hidden / bn);
+  CUtensorMap mc0;
+  if ((st = G::make_out_map(&mc0, dh1, max_rows, 2 * hidden, 2 * hidden))) return st;
+  p.tma_store = 1;
   cudaStream_t s = fk::as_stream(stream);
-  FK_BN_SWITCH(bn, return G::launch<BN_, false, true, G::MODE_M, G::EPI_SWIGLU_BWD>(ma, mb, p, max_tiles, s));
+  FK_BN_SWITCH(bn, return G::launch<BN_, false, true, G::MODE_M, G::EPI_SWIGLU_BWD>(ma, mb, mc0, mc0, p, max_tiles, s));
   return FK_OK;
 }
 
@@ -650,8 +735,11 @@ extern "C" int fk_moe_gemm_up_dgrad(const void* dh1, int64_t max_rows, int hidde
   p.ld0 = dim;
   p.err = err_flag;
   const int max_tiles = (int)(max_rows / G::BM) * (dim / bn);
+  CUtensorMap mc0;
+  if ((st = G::make_out_map(&mc0, dxs, max_rows, dim, dim))) return st;
+  p.tma_store = 1;
   cudaStream_t s = fk::as_stream(stream);
-  FK_BN_SWITCH(bn, return G::launch<BN_, false, true, G::MODE_M, G::EPI_STORE>(ma, mb, p, max_tiles, s));
+  FK_BN_SWITCH(bn, return G::launch<BN_, false, true, G::MODE_M, G::EPI_STORE>(ma, mb, mc0, mc0, p, max_tiles, s));
   return FK_OK;
 }
 
@@ -682,7 +770,12 @@ extern "C" int fk_moe_gemm_wgrad(const void* a, int m_dim, const void* b, int n_
   p.ld0 = n_dim;
   p.err = err_flag;
   const int max_tiles = n_experts * ((m_dim + G::BM - 1) / G::BM) * (n_dim / bn);
+  // TMA stores need every 128-row tile inside one expert's [m_dim, n_dim] block.
+  CUtensorMap mc0;
+  p.tma_store = (m_dim % G::BM == 0) ? 1 : 0;
+  if (p.tma_store && (st = G::make_out_map(&mc0, dw, (int64_t)n_experts * m_dim, n_dim, n_dim))) return st;
+  if (!p.tma_store) mc0 = ma;  // unused
   cudaStream_t s = fk::as_stream(stream);
-  FK_BN_SWITCH(bn, return G::launch<BN_, true, true, G::MODE_K, G::EPI_STORE>(ma, mb, p, max_tiles, s));
+  FK_BN_SWITCH(bn, return G::launch<BN_, true, true, G::MODE_K, G::EPI_STORE>(ma, mb, mc0, mc0, p, max_tiles, s));
   return FK_OK;
 }

@@ -18,7 +18,7 @@
 // which a log2(KP)-step bitonic merge sorts again -- first across the V registers of a
 // lane (no shuffles), then across lanes.  Work is O(L log^2 KP) instead of the
 // O(L log^2 L) of a full sort.  For k > S a full bitonic sort of all L keys is used.
-// Two rows are processed per warp pass when V <= 2 (independent shuffle chains), and the
+// Up to four rows are processed per warp pass (independent shuffle chains), and the
 // next pass's logits are loaded before the current pass's network runs.
 //
 // Weights.  The renormalised top-k softmax equals a softmax over the k selected logits:
@@ -137,23 +137,21 @@ __global__ void __launch_bounds__(256) router_fwd_kernel(const T* __restrict__ l
   const int64_t n_warps = ((int64_t)gridDim.x * blockDim.x) >> 5;
   const int64_t n_groups = (n_rows + RPW * RPI - 1) / (RPW * RPI);
 
-  auto load = [&](float (&x)[RPI][V], int64_t g) {
-#pragma unroll
-    for (int q = 0; q < RPI; ++q) {
-      const int64_t row = (g * RPI + q) * RPW + seg;
-#pragma unroll
-      for (int r = 0; r < V; ++r) {
-        const int e = r * S + lane_s;
-        x[q][r] = (g < n_groups && row < n_rows && e < E)
-                      ? Elt<T>::to_f(logits[row * row_stride + e]) : 0.f;
-      }
-    }
-  };
+  // Logits of group g into x (registers); zeros past the end.
+#define FK_ROUTER_LOAD(x, g)                                                            \
+  _Pragma("unroll") for (int q = 0; q < RPI; ++q) {                                     \
+    const int64_t row_ = ((g) * RPI + q) * RPW + seg;                                   \
+    _Pragma("unroll") for (int r = 0; r < V; ++r) {                                     \
+      const int e_ = r * S + lane_s;                                                    \
+      x[q][r] = ((g) < n_groups && row_ < n_rows && e_ < E)                             \
+                    ? Elt<T>::to_f(logits[row_ * row_stride + e_]) : 0.f;               \
+    }                                                                                   \
+  }
   float cur[RPI][V];
-  load(cur, warp_global);
+  FK_ROUTER_LOAD(cur, warp_global)
   for (int64_t g = warp_global; g < n_groups; g += n_warps) {
     float nxt[RPI][V];
-    load(nxt, g + n_warps);  // next group's logits in flight during this group's sort
+    FK_ROUTER_LOAD(nxt, g + n_warps)  // next group's logits in flight during this group's sort
     uint64_t top[RPI], keyv[RPI][V];
 #pragma unroll
     for (int q = 0; q < RPI; ++q) {
@@ -239,6 +237,7 @@ __global__ void __launch_bounds__(256) router_fwd_kernel(const T* __restrict__ l
 #pragma unroll
       for (int r = 0; r < V; ++r) cur[q][r] = nxt[q][r];
   }
+#undef FK_ROUTER_LOAD
 }
 
 // Backward: dense fp32 rows; selected entries get w_j * (dw_j - <w, dw>), others 0.
@@ -304,7 +303,7 @@ inline int warp_grid(int64_t n_groups) {
 template <typename T, int S, int V>
 int launch_gm(const T* lp, int64_t rs, int64_t n, int E, int k, float* w, int64_t* idx,
               cudaStream_t st) {
-  constexpr int RPI = (V <= 2) ? 2 : 1;
+  constexpr int RPI = (V <= 2) ? 4 : (V == 4 ? 2 : 1);
   const int64_t groups = (n + (32 / S) * RPI - 1) / ((32 / S) * RPI);
   const int grid = warp_grid(groups);
   const int KP = pow2_at_least(k);

@@ -146,7 +146,7 @@ def _ep_worker(rank, world, port, q):
         out = ep(x)
         out.backward(d_all[rank * T:(rank + 1) * T].to(dev))
         torch.cuda.synchronize()
-        q.put((rank, out.float().cpu(), x.grad.float().cpu()))
+        q.put((rank, out.detach().float().cpu(), x.grad.detach().float().cpu()))
     except Exception as exc:
         q.put((rank, repr(exc), None))
     finally:
@@ -164,7 +164,7 @@ def test_ep_layer_two_ranks_matches_single_gpu():
     procs = [ctx.Process(target=_ep_worker, args=(r, world, port, q)) for r in range(world)]
     for p in procs:
         p.start()
-    res = sorted([q.get(timeout=300) for _ in procs], key=lambda r: r[0])
+    res = sorted([q.get(timeout=180) for _ in procs], key=lambda r: r[0])
     for p in procs:
         p.join(timeout=60)
     for r in res:

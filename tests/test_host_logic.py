@@ -41,3 +41,11 @@ def test_moe_layers_keep_reference_parameters():
     masked.load_state_dict(sd)
     assert masked.w13.data_ptr() == masked.experts[0].w_gate.weight.data_ptr()
     assert all(p.is_leaf for p in masked.parameters())
+
+
+def test_mini_gpt_builds_both_modes():
+    from fusedkernels_b200.mini_gpt import MiniGPT
+    for fused in (True, False):
+        m = MiniGPT(vocab_size=64, dim=32, n_layers=2, n_heads=4, hidden_dim=48, max_seq_len=16,
+                    fused=fused)
+        assert sum(p.numel() for p in m.parameters()) > 0
