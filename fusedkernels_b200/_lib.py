@@ -51,6 +51,9 @@ SIGNATURES: dict[str, list] = {
     "fk_ep_pack": [_vp, _i32, _vp, _i64, _vp, _i32, _vp],
     "fk_ep_unpack_sum": [_vp, _i32, _vp, _i64, _i32, _vp, _i32, _vp],
     "fk_ep_unpack_dw": [_vp, _vp, _vp, _vp, _i64, _i32, _i32, _i32, _vp, _vp],
+    "fk_bitonic_sort_i32": [_vp, _i64, _i32, _i64, _vp, _i64, _vp],
+    "fk_bitonic_sort_bounded_i32": [_vp, _i64, _i32, _i64, _i32, _vp, _vp],
+    "fk_bitonic_merge_topk_i32": [_vp, _vp, _i64, _i32, _vp, _vp],
 }
 _RESTYPES = {"fk_status_string": C.c_char_p, "fk_last_error": C.c_char_p}
 

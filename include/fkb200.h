@@ -242,6 +242,22 @@ FK_API int fk_ep_unpack_dw(const float* back_dw, const int64_t* idx, const int* 
                            const int* src_pos, int64_t n_tokens, int k, int n_ranks,
                            int n_experts, float* dw, void* stream);
 
+/* ---------------------------------------------------------------- bitonic utilities
+ * int32 row sorts in shared memory, one CTA per row, rows of at most 2048 keys.
+ * fk_bitonic_sort_i32: each row ascending (replaces _bitonic_sort_ascending_kernel,
+ *   _bitonic_primitive.py:17-76).
+ * fk_bitonic_sort_bounded_i32: rows padded to next_pow2(width) with -2^30, every run of
+ *   `run` keys sorted ascending, out [n_rows, next_pow2(width)] (replaces
+ *   _bitonic_sort_bounded_kernel, _bitonic_primitive.py:79-164).
+ * fk_bitonic_merge_topk_i32: top kp of the union of two ascending rows, ascending
+ *   (replaces _bitonic_merge_topk_kernel, _bitonic_merge_primitive.py:31-85). */
+FK_API int fk_bitonic_sort_i32(const int* x, int64_t n_rows, int width, int64_t row_stride,
+                               int* out, int64_t out_stride, void* stream);
+FK_API int fk_bitonic_sort_bounded_i32(const int* x, int64_t n_rows, int width,
+                                       int64_t row_stride, int run, int* out, void* stream);
+FK_API int fk_bitonic_merge_topk_i32(const int* a, const int* b, int64_t n_rows, int kp,
+                                     int* out, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
