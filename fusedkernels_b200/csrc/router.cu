@@ -18,7 +18,7 @@
 // which a log2(KP)-step bitonic merge sorts again -- first across the V registers of a
 // lane (no shuffles), then across lanes.  Work is O(L log^2 KP) instead of the
 // O(L log^2 L) of a full sort.  For k > S a full bitonic sort of all L keys is used.
-// Up to four rows are processed per warp pass (independent shuffle chains), and the
+// Two rows are processed per warp pass when V <= 2 (independent shuffle chains), and the
 // next pass's logits are loaded before the current pass's network runs.
 //
 // Weights.  The renormalised top-k softmax equals a softmax over the k selected logits:
@@ -303,7 +303,7 @@ inline int warp_grid(int64_t n_groups) {
 template <typename T, int S, int V>
 int launch_gm(const T* lp, int64_t rs, int64_t n, int E, int k, float* w, int64_t* idx,
               cudaStream_t st) {
-  constexpr int RPI = (V <= 2) ? 4 : (V == 4 ? 2 : 1);
+  constexpr int RPI = (V <= 2) ? 2 : 1;
   const int64_t groups = (n + (32 / S) * RPI - 1) / ((32 / S) * RPI);
   const int grid = warp_grid(groups);
   const int KP = pow2_at_least(k);
