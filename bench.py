@@ -859,6 +859,51 @@ def run_reference(args):
     print(json.dumps(out), flush=True)
 
 
+def run_breakdown(args, reps=5):
+    """Per-call device time of one step: every C-ABI call of the step is bracketed by CUDA
+    events (eager launches), averaged over `reps` steps."""
+    import collections
+    from fusedkernels_b200 import _lib
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    torch.cuda.set_device(dev)
+    wl = Router(args.router_rows) if args.workload == "router" else WORKLOADS[args.workload]()
+    wl.setup(dev)
+    for _ in range(max(args.warmup, 3)):
+        wl.step()
+    torch.cuda.synchronize()
+    orig = _lib.call
+    rec = []
+
+    def timed(name, *a):
+        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s0.record()
+        orig(name, *a)
+        s1.record()
+        rec.append((name, s0, s1))
+
+    _lib.call = timed
+    tot, cnt, step_ms = collections.defaultdict(float), collections.Counter(), 0.0
+    try:
+        for _ in range(reps):
+            rec.clear()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            wl.step()
+            b.record()
+            torch.cuda.synchronize()
+            step_ms += a.elapsed_time(b) / reps
+            for n, s0, s1 in rec:
+                tot[n] += s0.elapsed_time(s1) / reps
+                cnt[n] += 1
+    finally:
+        _lib.call = orig
+    print(f"| call | launches | ms / step |\n|---|---|---|")
+    for n, t in sorted(tot.items(), key=lambda kv: -kv[1]):
+        print(f"| {n} | {cnt[n] // reps} | {t:.3f} |")
+    print(f"| sum of C-ABI calls | | {sum(tot.values()):.3f} |")
+    print(f"| whole eager step | | {step_ms:.3f} |")
+
+
 def wl_setup_host(wl):
     """Build the workload's host tensors without a GPU (for the CPU reference arm)."""
     G = gen(0)
@@ -927,11 +972,16 @@ def main():
     ap.add_argument("--rows", type=int, default=0,
                     help="override the row count of rmsnorm/swiglu/ce (profiling runs only)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--breakdown", action="store_true",
+                    help="print the device time of every C-ABI call in one step (eager, CUDA "
+                         "events around each call) instead of the JSON line")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
         run_reference(args)
+    elif args.breakdown:
+        run_breakdown(args)
     else:
         run_ours(args)
 
