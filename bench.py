@@ -49,13 +49,21 @@ def peaks():
                 "bf16_tflops_sustained": 1400.0, "source": "fallback"}
 
 
-def ncu_traffic(kernel_key):
-    """Per-launch DRAM bytes (read+write) of a kernel from a committed ncu summary."""
+def ncu_traffic(kernel_key, size_key):
+    """Per-launch DRAM bytes (read+write) of a kernel at one workload size, from the
+    committed ncu summary (keys "<kernel>@<size>"); None when that size was not captured."""
     try:
         t = json.loads(TRAFFIC_PATH.read_text())
-        return t[kernel_key]["dram_bytes_per_launch"]
+        return t[f"{kernel_key}@{size_key}"]["dram_bytes_per_launch"]
     except Exception:
         return None
+
+
+def l2_note(nbytes, what):
+    mb = nbytes / 1e6
+    if nbytes > 126e6:
+        return f"inputs exceed L2 ({what} {mb:.0f} MB > 126 MB)"
+    return f"inputs fit in L2 ({what} {mb:.0f} MB): repeated steps may be served from L2"
 
 
 class ClockSampler:
@@ -247,7 +255,10 @@ class RMSNorm(Workload):
     def config(self):
         return {"workload": "rmsnorm_fwd_bwd", "shape": [self.rows, self.cols], "x_dtype": "bf16",
                 "weight_dtype": "fp32", "eps": 1e-6,
-                "l2": "inputs exceed L2 (x, dy 134 MB each > 126 MB)"}
+                "l2": l2_note(self.rows * self.cols * 2, "x, dy each")}
+
+    def size_key(self):
+        return f"{self.rows}x{self.cols}"
 
 
 class SwiGLU(Workload):
@@ -327,7 +338,10 @@ class SwiGLU(Workload):
 
     def config(self):
         return {"workload": "swiglu_fwd_bwd", "shape": [self.rows, self.cols], "dtype": "bf16",
-                "l2": "inputs exceed L2 (470 MB per tensor)"}
+                "l2": l2_note(self.rows * self.cols * 2, "per tensor")}
+
+    def size_key(self):
+        return f"{self.rows}x{self.cols}"
 
 
 class CrossEntropy(Workload):
@@ -411,7 +425,10 @@ class CrossEntropy(Workload):
     def config(self):
         return {"workload": "cross_entropy_fwd_bwd", "shape": [self.rows, self.cols],
                 "dtype": "bf16", "ignore_fraction": 0.05, "inplace_grad": True,
-                "l2": "inputs exceed L2 (2.1 GB logits)"}
+                "l2": l2_note(self.rows * self.cols * 2, "logits")}
+
+    def size_key(self):
+        return f"{self.rows}x{self.cols}"
 
 
 class Router(Workload):
@@ -424,8 +441,8 @@ class Router(Workload):
     E, k = 64, 2
     graph_inner = 20
 
-    def __init__(self, rows=4096):
-        self.rows = rows
+    def __init__(self, rows=4096, experts=64, k=2):
+        self.rows, self.E, self.k = rows, experts, k
 
     def setup(self, dev):
         from fusedkernels_b200 import _lib
@@ -493,8 +510,12 @@ class Router(Workload):
     def config(self):
         return {"workload": "moe_router_fwd_bwd", "shape": [self.rows, self.E], "k": self.k,
                 "dtype": "fp32",
-                "l2": "inputs fit in L2 (1 MB); launch-latency bound" if self.rows <= 16384 else
-                      "inputs 33 MB: HBM/L2 streaming"}
+                "l2": (f"inputs {self.rows * self.E * 4 / 1e6:.0f} MB: "
+                       + ("fit in L2; launch-latency bound" if self.rows * self.E * 4 < 16e6
+                          else "HBM/L2 streaming"))}
+
+    def size_key(self):
+        return f"{self.rows}x{self.E}k{self.k}"
 
 
 class MoELayer(Workload):
@@ -506,6 +527,7 @@ class MoELayer(Workload):
     (token, expert) assignments (2*M*K*N each) plus the router GEMM fwd+bwd."""
     name = "moe"
     metric = "MoE layer fwd+bwd throughput"
+    ep_transport = "peer"
     unit = "tokens/s"
     strong = True  # the 32768 global tokens are split across ranks
     tokens, dim, hidden, E, k = 32768, 4096, 1024, 128, 8
@@ -547,7 +569,8 @@ class MoELayer(Workload):
                 _, idx = fk.fused_moe_route_v2(logits, self.k)
                 load = torch.bincount(idx.reshape(-1), minlength=E).float().cpu()
             self.placement = lpt_placement(load.tolist(), self.world)
-            layer = ExpertParallelMoEMLP(D, H, E, self.k, placement=self.placement).to(dev).bfloat16()
+            layer = ExpertParallelMoEMLP(D, H, E, self.k, placement=self.placement,
+                                         transport=self.ep_transport).to(dev).bfloat16()
             layer.load_from_full(wr, wg, wu, wd)
             per = self.tokens // self.world
             T0, T1 = self.rank * per, (self.rank + 1) * per
@@ -645,11 +668,16 @@ class MoELayer(Workload):
     def config(self):
         par = "single GPU" if self.world == 1 else (
             f"ep{self.world}: {self.E // self.world} experts per GPU, load-aware (LPT) static "
-            f"placement, all-to-all dispatch/combine; {self.tokens // self.world} tokens per GPU")
+            f"placement, dispatch/combine "
+            + ("by put kernels into peer memory over NVLink" if self.ep_transport == "peer"
+               else "by NCCL all-to-all") + f"; {self.tokens // self.world} tokens per GPU")
         return {"workload": "moe_sorted_dispatch_fwd_bwd", "tokens": self.tokens, "dim": self.dim,
                 "hidden": self.hidden, "n_experts": self.E, "k": self.k, "dtype": "bf16",
                 "router_bias": "2*ln(zipf(1.1) rank weights)", "parallelism": par,
                 "l2": "inputs exceed L2 (x 268 MB, expert weights 3.2 GB)"}
+
+    def size_key(self):
+        return f"{self.tokens}x{self.dim}e{self.E}k{self.k}"
 
 
 def moe_cpu_sample(wl, n_tok):
@@ -702,6 +730,12 @@ def max_over_ranks(v, dev):
     return float(t.item())
 
 
+def make_workload(args):
+    if args.workload == "router":
+        return Router(args.router_rows, args.router_experts, args.router_k)
+    return WORKLOADS[args.workload]()
+
+
 def run_ours(args):
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -712,10 +746,11 @@ def run_ours(args):
         import datetime
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                              device_id=dev)
-    wl = Router(args.router_rows) if args.workload == "router" else WORKLOADS[args.workload]()
+    wl = make_workload(args)
     if args.rows and hasattr(wl, "rows") and args.workload != "router":
         wl.rows = args.rows
     if args.workload == "moe":
+        wl.ep_transport = args.ep_transport
         if args.moe_tokens:
             wl.tokens = args.moe_tokens
         if args.moe_experts:
@@ -779,11 +814,11 @@ def run_ours(args):
             kk["flops"] = kk.pop("bytes")
         roof = {"bound": "tensor", "achieved": dom["tflops"], "peak": pk["bf16_tflops"],
                 "unit": "TFLOP/s", "frac": round(dom["tflops"] / pk["bf16_tflops"], 4),
-                "traffic": ncu_traffic(dom["kernel"]), "kernel": dom["kernel"],
+                "traffic": ncu_traffic(dom["kernel"], wl.size_key()), "kernel": dom["kernel"],
                 "peak_source": pk["source"] + " (burst: kernel timed alone)"}
     else:
         roof = {"bound": "hbm", "achieved": dom["gbs"], "peak": pk["hbm_gbs"], "unit": "GB/s",
-                "frac": round(dom["gbs"] / pk["hbm_gbs"], 4), "traffic": ncu_traffic(dom["kernel"]),
+                "frac": round(dom["gbs"] / pk["hbm_gbs"], 4), "traffic": ncu_traffic(dom["kernel"], wl.size_key()),
                 "kernel": dom["kernel"], "peak_source": pk["source"]}
 
     # End to end through the public API with host buffers.
@@ -826,6 +861,9 @@ def run_ours(args):
     import gc
     gc.collect()
     if torch.distributed.is_initialized():
+        layer = getattr(wl, "layer", None)
+        if hasattr(layer, "close"):
+            layer.close()  # collective: unmaps the peer-memory exchange regions
         torch.distributed.barrier()
         torch.distributed.destroy_process_group()
 
@@ -834,7 +872,7 @@ def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    wl = Router(args.router_rows) if args.workload == "router" else WORKLOADS[args.workload]()
+    wl = make_workload(args)
     # Host-only setup: the CPU reference never touches the GPU.
     wl_setup_host(wl)
     cores = len(os.sched_getaffinity(0))
@@ -866,7 +904,7 @@ def run_breakdown(args, reps=5):
     from fusedkernels_b200 import _lib
     dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
     torch.cuda.set_device(dev)
-    wl = Router(args.router_rows) if args.workload == "router" else WORKLOADS[args.workload]()
+    wl = make_workload(args)
     wl.setup(dev)
     for _ in range(max(args.warmup, 3)):
         wl.step()
@@ -967,10 +1005,14 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="rmsnorm")
     ap.add_argument("--router-rows", type=int, default=4096)
+    ap.add_argument("--router-experts", type=int, default=64, help="profiling runs only")
+    ap.add_argument("--router-k", type=int, default=2, help="profiling runs only")
     ap.add_argument("--moe-tokens", type=int, default=0, help="profiling runs only")
     ap.add_argument("--moe-experts", type=int, default=0, help="profiling runs only")
     ap.add_argument("--rows", type=int, default=0,
                     help="override the row count of rmsnorm/swiglu/ce (profiling runs only)")
+    ap.add_argument("--ep-transport", choices=["peer", "nccl"], default="peer",
+                    help="token exchange of the expert-parallel MoE layer (N > 1)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--breakdown", action="store_true",
                     help="print the device time of every C-ABI call in one step (eager, CUDA "

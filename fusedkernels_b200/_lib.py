@@ -51,6 +51,15 @@ SIGNATURES: dict[str, list] = {
     "fk_ep_pack": [_vp, _i32, _vp, _i64, _vp, _i32, _vp],
     "fk_ep_unpack_sum": [_vp, _i32, _vp, _i64, _i32, _vp, _i32, _vp],
     "fk_ep_unpack_dw": [_vp, _vp, _vp, _vp, _i64, _i32, _i32, _i32, _vp, _vp],
+    "fk_ipc_alloc": [_sz, C.POINTER(_vp), _vp],
+    "fk_ipc_open": [_vp, C.POINTER(_vp)],
+    "fk_ipc_close": [_vp],
+    "fk_ipc_free": [_vp],
+    "fk_ep_peer_put_rows": [_vp, _i32, _vp, _i64, _i32, _i32, _vp, _vp, _i32, _vp, _vp, _vp, _vp,
+                            _i32, _vp, _i32, _vp],
+    "fk_ep_peer_combine_put": [_vp, _i32, _vp, _vp, _i64, _i32, _i32, _i32, _vp, _vp, _vp, _vp,
+                               _i32, _vp, _i32, _vp],
+    "fk_ep_peer_wait": [_vp, _i32, _i32, _vp, _i32, _vp, _vp],
     "fk_bitonic_sort_i32": [_vp, _i64, _i32, _i64, _vp, _i64, _vp],
     "fk_bitonic_sort_bounded_i32": [_vp, _i64, _i32, _i64, _i32, _vp, _vp],
     "fk_bitonic_merge_topk_i32": [_vp, _vp, _i64, _i32, _vp, _vp],

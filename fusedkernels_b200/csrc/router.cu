@@ -8,6 +8,12 @@
 // exact logit and breaks ties toward the LOWER expert index.  Padding slots get key 0,
 // which is below every real key (-inf maps to 0x007FFFFF in the high word).
 //
+// Two kernel families.  For k <= 8 (every routing configuration of the reference's
+// tests and benchmarks; k <= 4 when E > 128) the forward holds a row in a small group of
+// lanes that each select over 8 logits by sorted insertion and merge their lists by a
+// butterfly (the lane-group kernels further down), and for k <= 4 the backward uses the
+// same lane groups.  Otherwise the segment kernels below run a bitonic network.
+//
 // Layout.  A row of E experts is padded to L = S*V (power of two) and held by a
 // segment of S lanes (S = min(32, L)), V keys per lane; element i = r*S + lane.
 // E <= 32 packs 32/S rows into each warp.
@@ -24,6 +30,8 @@
 // Weights.  The renormalised top-k softmax equals a softmax over the k selected logits:
 // w_j = exp(x_j - m) / sum_{i in top-k} exp(x_i - m), with m the largest logit (the
 // full-E denominator cancels), so only k exponentials are needed per row.
+#include <climits>
+
 #include "common.cuh"
 
 namespace fk {
@@ -240,6 +248,255 @@ __global__ void __launch_bounds__(256) router_fwd_kernel(const T* __restrict__ l
 #undef FK_ROUTER_LOAD
 }
 
+// ---------------------------------------------------------------------------------------
+// Lane-group kernels, k <= 8.  A row is held by a group of G lanes (G = next_pow2(E/8),
+// 1..32), 8 logits per lane: lane l of the group owns the 16-byte packets p*G + l of the
+// row (2 packets of fp32 or 1 of bf16/fp16), so one warp load covers 32/G whole rows.
+// Each lane keeps the top KP = next_pow2(k) (key, expert) pairs of its 8 logits in
+// registers by sorted insertion -- its logits arrive in increasing expert order, so a
+// strict '>' keeps the lower index first on ties -- and the G lists are merged by a
+// butterfly over the group: at distance d the partner's list is reversed, the pairwise
+// better of the two lists is a bitonic sequence holding the top KP of both, and a
+// log2(KP)-step bitonic merge sorts it again.  The comparator (key desc, expert asc) is a
+// total order, so every lane of the group ends with the same list.  Per row this costs
+// about E*(KP+3) ALU operations and 2*KP*log2(G) shuffles per lane, against the
+// shuffle-bound O(E log^2 KP) network of the segment kernel above.
+//
+// Keys are signed integers: bits ^ ((bits >> 31) & 0x7fffffff) orders like the float and
+// is its own inverse; -0.0 is folded onto +0.0 (x + 0.0f) and every NaN becomes INT_MAX,
+// above +inf (0x7f800000).  Padding is INT_MIN, below -inf (0x807fffff).
+constexpr int kLaneElems = 8;   // logits per lane
+constexpr int kLaneMaxKP = 8;   // largest list kept per lane
+
+__device__ __forceinline__ int skey(float x) {
+  x = x + 0.0f;
+  int s = __float_as_int(x);
+  s ^= (s >> 31) & 0x7fffffff;
+  return (x != x) ? 0x7fffffff : s;
+}
+
+__device__ __forceinline__ float skey_value(int s) {
+  return __int_as_float(s ^ ((s >> 31) & 0x7fffffff));
+}
+
+__device__ __forceinline__ bool better(int va, int ia, int vb, int ib) {
+  return va > vb || (va == vb && ia < ib);
+}
+
+// Insert (v, e) into the descending list kv/ki; e is larger than every index already in it.
+template <int KP>
+__device__ __forceinline__ void insert_sorted(int (&kv)[KP], int (&ki)[KP], int v, int e) {
+  bool c[KP];
+#pragma unroll
+  for (int i = 0; i < KP; ++i) c[i] = v > kv[i];
+#pragma unroll
+  for (int i = KP - 1; i > 0; --i) {
+    kv[i] = c[i - 1] ? kv[i - 1] : (c[i] ? v : kv[i]);
+    ki[i] = c[i - 1] ? ki[i - 1] : (c[i] ? e : ki[i]);
+  }
+  kv[0] = c[0] ? v : kv[0];
+  ki[0] = c[0] ? e : ki[0];
+}
+
+// Replace the list by the top KP of it and the list of the lane at xor distance d.
+template <int KP>
+__device__ __forceinline__ void merge_xor(int (&kv)[KP], int (&ki)[KP], int d) {
+  int bv[KP], bi[KP];
+#pragma unroll
+  for (int i = 0; i < KP; ++i) {
+    bv[i] = __shfl_xor_sync(0xffffffffu, kv[i], d);
+    bi[i] = __shfl_xor_sync(0xffffffffu, ki[i], d);
+  }
+#pragma unroll
+  for (int i = 0; i < KP; ++i) {
+    const int j = KP - 1 - i;
+    const bool t = better(kv[i], ki[i], bv[j], bi[j]);
+    kv[i] = t ? kv[i] : bv[j];
+    ki[i] = t ? ki[i] : bi[j];
+  }
+#pragma unroll
+  for (int s = KP >> 1; s > 0; s >>= 1) {
+#pragma unroll
+    for (int i = 0; i < KP; ++i) {
+      if ((i & s) == 0) {
+        const bool t = better(kv[i], ki[i], kv[i + s], ki[i + s]);
+        const int av = kv[i], ai = ki[i];
+        kv[i] = t ? av : kv[i + s];
+        ki[i] = t ? ai : ki[i + s];
+        kv[i + s] = t ? kv[i + s] : av;
+        ki[i + s] = t ? ki[i + s] : ai;
+      }
+    }
+  }
+}
+
+template <typename T, int G, bool VEC>
+__device__ __forceinline__ void lanes_load(const T* __restrict__ logits, int64_t row_stride,
+                                           int64_t row, bool ok, int E, int l,
+                                           float (&x)[kLaneElems]) {
+  constexpr int VN = 16 / (int)sizeof(T);
+  constexpr int P = kLaneElems / VN;
+  const T* rp = logits + row * row_stride;
+#pragma unroll
+  for (int p = 0; p < P; ++p) {
+    const int e0 = (p * G + l) * VN;
+    if constexpr (VEC) {
+      if (ok && e0 < E) {
+        const Vec16<T> v = ld_keep(rp + e0);
+#pragma unroll
+        for (int q = 0; q < VN; ++q) x[p * VN + q] = Elt<T>::to_f(v.e[q]);
+      } else {
+#pragma unroll
+        for (int q = 0; q < VN; ++q) x[p * VN + q] = 0.f;
+      }
+    } else {
+#pragma unroll
+      for (int q = 0; q < VN; ++q)
+        x[p * VN + q] = (ok && e0 + q < E) ? Elt<T>::to_f(rp[e0 + q]) : 0.f;
+    }
+  }
+}
+
+template <typename T, int G, int KP, bool VEC>
+__global__ void __launch_bounds__(256) router_fwd_lanes(const T* __restrict__ logits,
+                                                        int64_t row_stride, int64_t n_rows,
+                                                        int E, int k, float* __restrict__ w_out,
+                                                        int64_t* __restrict__ idx_out) {
+  constexpr int VN = 16 / (int)sizeof(T);
+  constexpr int P = kLaneElems / VN;
+  constexpr int RPW = 32 / G;  // rows per warp per pass
+  const int lane = threadIdx.x & 31;
+  const int l = lane % G;
+  const int grp = lane / G;
+  const int64_t warp_global = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int64_t n_warps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  const int64_t n_tiles = (n_rows + RPW - 1) / RPW;
+
+  float cur[kLaneElems];
+  {
+    const int64_t row = warp_global * RPW + grp;
+    lanes_load<T, G, VEC>(logits, row_stride, row, warp_global < n_tiles && row < n_rows, E, l,
+                          cur);
+  }
+  // The tile loop is warp-uniform: every lane reaches every shuffle.
+  for (int64_t tile = warp_global; tile < n_tiles; tile += n_warps) {
+    const int64_t row = tile * RPW + grp;
+    const bool row_ok = row < n_rows;
+    float nxt[kLaneElems];
+    {
+      const int64_t nt = tile + n_warps;
+      const int64_t nrow = nt * RPW + grp;
+      lanes_load<T, G, VEC>(logits, row_stride, nrow, nt < n_tiles && nrow < n_rows, E, l, nxt);
+    }
+    int kv[KP], ki[KP];
+#pragma unroll
+    for (int i = 0; i < KP; ++i) {
+      kv[i] = INT_MIN;
+      ki[i] = INT_MAX;
+    }
+#pragma unroll
+    for (int p = 0; p < P; ++p) {
+#pragma unroll
+      for (int q = 0; q < VN; ++q) {
+        const int e = (p * G + l) * VN + q;
+        const int v = (row_ok && e < E) ? skey(cur[p * VN + q]) : INT_MIN;
+        insert_sorted<KP>(kv, ki, v, e);
+      }
+    }
+#pragma unroll
+    for (int d = 1; d < G; d <<= 1) merge_xor<KP>(kv, ki, d);
+
+    const float m = skey_value(kv[0]);
+    float ex[KP];
+    float ssum = 0.f;
+#pragma unroll
+    for (int i = 0; i < KP; ++i) {
+      ex[i] = 0.f;
+      if (i < k) {
+        ex[i] = expf(skey_value(kv[i]) - m);
+        ssum += ex[i];
+      }
+    }
+    if (row_ok) {
+      const float inv = 1.0f / ssum;
+      for (int j = l; j < k; j += G) {
+        float exj = ex[0];
+        int ij = ki[0];
+#pragma unroll
+        for (int i = 1; i < KP; ++i)
+          if (i == j) {
+            exj = ex[i];
+            ij = ki[i];
+          }
+        w_out[row * k + j] = exj * inv;
+        idx_out[row * k + j] = (int64_t)ij;
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < kLaneElems; ++i) cur[i] = nxt[i];
+  }
+}
+
+// Backward with the same row/lane mapping: lane l writes the fp32 packets p*G + l of the
+// dense gradient row; an expert listed twice takes the later slot's value.
+template <int G, int KP, bool VEC>
+__global__ void __launch_bounds__(256) router_bwd_lanes(const float* __restrict__ dw,
+                                                        const float* __restrict__ w,
+                                                        const int64_t* __restrict__ idx,
+                                                        float* __restrict__ dlogits,
+                                                        int64_t n_rows, int E, int k) {
+  constexpr int P = kLaneElems / 4;
+  constexpr int RPW = 32 / G;
+  const int lane = threadIdx.x & 31;
+  const int l = lane % G;
+  const int grp = lane / G;
+  const int64_t warp_global = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int64_t n_warps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  const int64_t n_tiles = (n_rows + RPW - 1) / RPW;
+  for (int64_t tile = warp_global; tile < n_tiles; tile += n_warps) {
+    const int64_t row = tile * RPW + grp;
+    if (row >= n_rows) continue;
+    float wv[KP], dv[KP], g[KP];
+    int id[KP];
+    float dot = 0.f;
+#pragma unroll
+    for (int i = 0; i < KP; ++i) {
+      wv[i] = 0.f;
+      dv[i] = 0.f;
+      id[i] = -1;
+      if (i < k) {
+        wv[i] = w[row * k + i];
+        dv[i] = dw[row * k + i];
+        const int64_t e = idx[row * k + i];
+        id[i] = (e >= 0 && e < E) ? (int)e : -1;
+        dot = fmaf(wv[i], dv[i], dot);
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < KP; ++i) g[i] = wv[i] * (dv[i] - dot);
+    float* rp = dlogits + row * E;
+#pragma unroll
+    for (int p = 0; p < P; ++p) {
+      const int e0 = (p * G + l) * 4;
+      float o[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        o[q] = 0.f;
+#pragma unroll
+        for (int i = 0; i < KP; ++i)
+          if (id[i] == e0 + q) o[q] = g[i];
+      }
+      if constexpr (VEC) {
+        if (e0 < E) *reinterpret_cast<float4*>(rp + e0) = make_float4(o[0], o[1], o[2], o[3]);
+      } else {
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          if (e0 + q < E) rp[e0 + q] = o[q];
+      }
+    }
+  }
+}
+
 // Backward: dense fp32 rows; selected entries get w_j * (dw_j - <w, dw>), others 0.
 template <int S, int V>
 __global__ void __launch_bounds__(256) router_bwd_kernel(const float* __restrict__ dw,
@@ -328,10 +585,72 @@ int launch_full(const T* lp, int64_t rs, int64_t n, int E, int k, float* w, int6
   return FK_OK;
 }
 
+inline int lanes_per_row(int E) {
+  const int g = pow2_at_least((E + kLaneElems - 1) / kLaneElems);
+  return g > 32 ? 32 : g;
+}
+
+// Persistent grid for a lane-group kernel: no more CTAs than are resident at once, so no
+// SM runs a second partial wave (the kernels are register-limited below 8 CTAs per SM).
+template <typename K>
+int resident_grid(K kernel, int64_t n_warp_tiles) {
+  static int per_sm = 0;  // one cached value per kernel instantiation
+  if (per_sm == 0) {
+    int b = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, kernel, 256, 0) != cudaSuccess || b < 1)
+      b = 1;
+    per_sm = b;
+  }
+  int64_t ctas = (n_warp_tiles + 7) / 8;
+  const int64_t cap = (int64_t)num_sms() * per_sm;
+  if (ctas > cap) ctas = cap;
+  return (int)(ctas < 1 ? 1 : ctas);
+}
+
+template <typename T, int G, int KP>
+void launch_lanes_fwd(const T* lp, int64_t rs, int64_t n, int E, int k, float* w, int64_t* idx,
+                      bool vec, cudaStream_t st) {
+  const int64_t tiles = (n + 32 / G - 1) / (32 / G);
+  if (vec) {
+    auto* kern = router_fwd_lanes<T, G, KP, true>;
+    kern<<<resident_grid(kern, tiles), 256, 0, st>>>(lp, rs, n, E, k, w, idx);
+  } else {
+    auto* kern = router_fwd_lanes<T, G, KP, false>;
+    kern<<<resident_grid(kern, tiles), 256, 0, st>>>(lp, rs, n, E, k, w, idx);
+  }
+}
+
+template <typename T, int KP>
+void lanes_fwd_g(const T* lp, int64_t rs, int64_t n, int E, int k, float* w, int64_t* idx,
+                 bool vec, cudaStream_t st) {
+  switch (lanes_per_row(E)) {
+    case 1: launch_lanes_fwd<T, 1, KP>(lp, rs, n, E, k, w, idx, vec, st); break;
+    case 2: launch_lanes_fwd<T, 2, KP>(lp, rs, n, E, k, w, idx, vec, st); break;
+    case 4: launch_lanes_fwd<T, 4, KP>(lp, rs, n, E, k, w, idx, vec, st); break;
+    case 8: launch_lanes_fwd<T, 8, KP>(lp, rs, n, E, k, w, idx, vec, st); break;
+    case 16: launch_lanes_fwd<T, 16, KP>(lp, rs, n, E, k, w, idx, vec, st); break;
+    default: launch_lanes_fwd<T, 32, KP>(lp, rs, n, E, k, w, idx, vec, st); break;
+  }
+}
+
 template <typename T>
 int fwd_t(const void* logits, int64_t rs, int64_t n, int E, int k, float* w, int64_t* idx,
           cudaStream_t st) {
   const T* lp = static_cast<const T*>(logits);
+  const int KPL = pow2_at_least(k);
+  // Measured on B200: the lane groups win for every k <= 8 up to E = 128; at 256 experts
+  // with k > 4 the 32-lane insertion chains lose to the segment network.
+  if (KPL <= kLaneMaxKP && !(KPL > 4 && lanes_per_row(E) == 32)) {
+    constexpr int VN = 16 / (int)sizeof(T);
+    const bool vec = aligned16(logits) && (rs * (int64_t)sizeof(T)) % 16 == 0 && E % VN == 0;
+    switch (KPL) {
+      case 1: lanes_fwd_g<T, 1>(lp, rs, n, E, k, w, idx, vec, st); break;
+      case 2: lanes_fwd_g<T, 2>(lp, rs, n, E, k, w, idx, vec, st); break;
+      case 4: lanes_fwd_g<T, 4>(lp, rs, n, E, k, w, idx, vec, st); break;
+      default: lanes_fwd_g<T, 8>(lp, rs, n, E, k, w, idx, vec, st); break;
+    }
+    return launch_status("fk_router_fwd");
+  }
   const int L = pow2_at_least(E);
   const int S = L < 32 ? L : 32;
   const int V = L / S;
@@ -389,12 +708,47 @@ extern "C" int fk_router_bwd(const float* dw, const float* w, const int64_t* idx
     return fk::fail(FK_ERR_UNSUPPORTED, "fk_router_bwd: n_experts=%d > 256", n_experts);
   if (n_rows == 0) return FK_OK;
   FK_CHECK_ARG(dw && w && idx && dlogits, "fk_router_bwd: null pointer");
+  cudaStream_t st = fk::as_stream(stream);
+  const int KPL = fk::pow2_at_least(k);
+  // Every lane reads all k slots of its row, so the lane groups are used for k <= 4 only
+  // (measured on B200: faster than the warp-per-row kernel there, slower at k = 8).
+  if (KPL <= 4) {
+    const int G = fk::lanes_per_row(n_experts);
+    const bool vec = fk::aligned16(dlogits) && n_experts % 4 == 0;
+    const int64_t tiles = (n_rows + 32 / G - 1) / (32 / G);
+#define FK_LANES(G_, KP_)                                                                  \
+  if (vec) {                                                                               \
+    auto* kern = fk::router_bwd_lanes<G_, KP_, true>;                                      \
+    kern<<<fk::resident_grid(kern, tiles), 256, 0, st>>>(dw, w, idx, dlogits, n_rows,      \
+                                                         n_experts, k);                    \
+  } else {                                                                                 \
+    auto* kern = fk::router_bwd_lanes<G_, KP_, false>;                                     \
+    kern<<<fk::resident_grid(kern, tiles), 256, 0, st>>>(dw, w, idx, dlogits, n_rows,      \
+                                                         n_experts, k);                    \
+  }
+#define FK_LANES_G(KP_)                  \
+  switch (G) {                           \
+    case 1: FK_LANES(1, KP_) break;      \
+    case 2: FK_LANES(2, KP_) break;      \
+    case 4: FK_LANES(4, KP_) break;      \
+    case 8: FK_LANES(8, KP_) break;      \
+    case 16: FK_LANES(16, KP_) break;    \
+    default: FK_LANES(32, KP_) break;    \
+  }
+    switch (KPL) {
+      case 1: FK_LANES_G(1) break;
+      case 2: FK_LANES_G(2) break;
+      default: FK_LANES_G(4) break;
+    }
+#undef FK_LANES_G
+#undef FK_LANES
+    return fk::launch_status("fk_router_bwd");
+  }
   const int L = fk::pow2_at_least(n_experts);
   const int S = L < 32 ? L : 32;
   const int V = L / S;
   const int64_t groups = (n_rows + (32 / S) - 1) / (32 / S);
   const int grid = fk::warp_grid(groups);
-  cudaStream_t st = fk::as_stream(stream);
 #define FK_LAUNCH(S_, V_) \
   fk::router_bwd_kernel<S_, V_><<<grid, 256, 0, st>>>(dw, w, idx, dlogits, n_rows, n_experts, k)
   if (S < 32) {

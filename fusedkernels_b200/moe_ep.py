@@ -59,7 +59,8 @@ def round_robin_placement(n_experts: int, n_ranks: int) -> list[int]:
 
 
 class Exchange:
-    """Fixed-capacity all-to-all of [n_ranks * cap, ...] buffers over a process group."""
+    """Fixed-capacity all-to-all of [n_ranks * cap, ...] buffers over a process group
+    (the NCCL transport)."""
 
     def __init__(self, group=None):
         self.group = group
@@ -70,6 +71,79 @@ class Exchange:
         recv = torch.empty_like(send)
         work = dist.all_to_all_single(recv, send, group=self.group, async_op=async_op)
         return (recv, work) if async_op else recv
+
+
+class PeerExchange:
+    """The NVLink transport: one exchange region per rank (allocated by the library, shared
+    with CUDA IPC, mapped into every other rank of the group, which must sit on one node),
+    written directly by the put kernels (see csrc/moe_ep_peer.cu for the protocol).
+
+    Regions (fixed-capacity layout of fk_ep_plan, T tokens per rank): to_expert
+    [N*T, dim] bf16, meta_e [N*T, k] int32, meta_w [N*T, k] fp32, to_source [N*T, dim]
+    bf16, dw [N*T, k] fp32, flags [4, N] uint32.  Creating and closing are collective."""
+
+    PHASE_FWD_DISPATCH, PHASE_FWD_COMBINE, PHASE_BWD_DISPATCH, PHASE_BWD_COMBINE = 0, 1, 2, 3
+
+    def __init__(self, group, n_tokens: int, dim: int, k: int, device, timeout_ms: int = 2000):
+        import ctypes as C
+        self.timeout_ms = timeout_ms
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.key = (n_tokens, dim, k)
+        N, T = self.world, n_tokens
+        sizes = [("to_expert", N * T * dim * 2), ("meta_e", N * T * k * 4),
+                 ("meta_w", N * T * k * 4), ("to_source", N * T * dim * 2),
+                 ("dw", N * T * k * 4), ("flags", 4 * N * 4)]
+        self.offset, total = {}, 0
+        for name, nbytes in sizes:
+            self.offset[name] = total
+            total += (nbytes + 255) // 256 * 256
+        own = C.c_void_p()
+        handle = C.create_string_buffer(64)
+        _lib.call("fk_ipc_alloc", total, C.byref(own), handle)
+        self._own = own.value
+        handles = [None] * N
+        dist.all_gather_object(handles, bytes(handle.raw), group=group)
+        self._opened = []
+        bases = []
+        for d in range(N):
+            if d == self.rank:
+                bases.append(self._own)
+                continue
+            p = C.c_void_p()
+            _lib.call("fk_ipc_open", C.create_string_buffer(handles[d], 64), C.byref(p))
+            self._opened.append(p.value)
+            bases.append(p.value)
+        self.tables = {name: torch.tensor([b + off for b in bases], dtype=torch.int64,
+                                          device=device)
+                       for name, off in self.offset.items()}
+        self.ctl = torch.zeros(24, dtype=torch.int32, device=device)
+        self.err = torch.zeros(1, dtype=torch.int32, device=device)
+        dist.barrier(group=group)  # every rank has mapped every region
+
+    def local(self, name: str) -> int:
+        return self._own + self.offset[name]
+
+    def table(self, name: str) -> int:
+        return self.tables[name].data_ptr()
+
+    def wait(self, phase: int, stream) -> None:
+        _lib.call("fk_ep_peer_wait", self.local("flags"), self.world, phase, self.ctl.data_ptr(),
+                  self.timeout_ms, self.err.data_ptr(), stream)
+
+    def close(self) -> None:
+        """Collective: unmap the peers' regions, then free this rank's region."""
+        if self._own is None:
+            return
+        torch.cuda.synchronize()
+        dist.barrier(group=self.group)
+        for p in self._opened:
+            _lib.call("fk_ipc_close", p)
+        self._opened = []
+        dist.barrier(group=self.group)
+        _lib.call("fk_ipc_free", self._own)
+        self._own = None
 
 
 def _pack_meta(e: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
@@ -103,17 +177,27 @@ class _EPMoEFn(torch.autograd.Function):
         _lib.call("fk_ep_plan", idx.data_ptr(), w.data_ptr(), T, k, layer.expert_rank.data_ptr(),
                   layer.expert_local.data_ptr(), E, N, send_token.data_ptr(), send_e.data_ptr(),
                   send_w.data_ptr(), src_pos.data_ptr(), send_count.data_ptr(), perr.data_ptr(), st)
-        send_x = torch.empty(N * T, d, dtype=torch.bfloat16, device=dev)
-        _lib.call("fk_ep_pack", x.data_ptr(), d, send_token.data_ptr(), N * T, send_x.data_ptr(),
-                  _lib.FK_BF16, st)
-        recv_x = ex.all_to_all(send_x)
-        recv_e, recv_w = _unpack_meta(ex.all_to_all(_pack_meta(send_e, send_w)), k)
+        px = layer._peer(T, d, k, dev) if layer.transport == "peer" else None
+        if px is not None:
+            _lib.call("fk_ep_peer_put_rows", x.data_ptr(), d, send_token.data_ptr(), T, N, ex.rank,
+                      send_e.data_ptr(), send_w.data_ptr(), k, px.table("to_expert"),
+                      px.table("meta_e"), px.table("meta_w"), px.table("flags"),
+                      px.PHASE_FWD_DISPATCH, px.ctl.data_ptr(), _lib.FK_BF16, st)
+            px.wait(px.PHASE_FWD_DISPATCH, st)
+            recv_x_p, recv_e_p, recv_w_p = px.local("to_expert"), px.local("meta_e"), px.local("meta_w")
+        else:
+            send_x = torch.empty(N * T, d, dtype=torch.bfloat16, device=dev)
+            _lib.call("fk_ep_pack", x.data_ptr(), d, send_token.data_ptr(), N * T,
+                      send_x.data_ptr(), _lib.FK_BF16, st)
+            recv_x = ex.all_to_all(send_x)
+            recv_e, recv_w = _unpack_meta(ex.all_to_all(_pack_meta(send_e, send_w)), k)
+            recv_x_p, recv_e_p, recv_w_p = recv_x.data_ptr(), recv_e.data_ptr(), recv_w.data_ptr()
         # local experts on the received rows (N*T "tokens" with k slots, -1 = not local)
         R_tok = N * T
         plan = _Plan(R_tok, k, El, dev)
         R = plan.max_rows
         eptr = plan.err.data_ptr()
-        _lib.call("fk_moe_route_meta_skip", recv_e.data_ptr(), recv_w.data_ptr(), R_tok, k, El,
+        _lib.call("fk_moe_route_meta_skip", recv_e_p, recv_w_p, R_tok, k, El,
                   plan.counts.data_ptr(), plan.seg_start.data_ptr(), plan.tile_expert.data_ptr(),
                   plan.n_mblk.data_ptr(), plan.sorted_assign.data_ptr(), plan.sorted_w.data_ptr(),
                   plan.slot_pos.data_ptr(), R, plan.ws.data_ptr(), plan.ws.numel(), eptr, st)
@@ -122,19 +206,27 @@ class _EPMoEFn(torch.autograd.Function):
         h1 = torch.empty(R, 2 * H, **bf)
         act = torch.empty(R, H, **bf)
         y = torch.empty(R, d, **bf)
-        partial = torch.empty(R_tok, d, **bf)
-        _lib.call("fk_moe_gather", recv_x.data_ptr(), d, plan.sorted_assign.data_ptr(), k,
+        _lib.call("fk_moe_gather", recv_x_p, d, plan.sorted_assign.data_ptr(), k,
                   plan.n_mblk.data_ptr(), R, xs.data_ptr(), _lib.FK_BF16, st)
         _lib.call("fk_moe_gemm_up", xs.data_ptr(), R, d, layer.w13.data_ptr(), H, El,
                   plan.tile_expert.data_ptr(), plan.n_mblk.data_ptr(), h1.data_ptr(),
                   act.data_ptr(), eptr + 4, st)
         _lib.call("fk_moe_gemm_down", act.data_ptr(), R, H, layer.w2.data_ptr(), d, El,
                   plan.tile_expert.data_ptr(), plan.n_mblk.data_ptr(), y.data_ptr(), eptr + 4, st)
-        _lib.call("fk_moe_combine", y.data_ptr(), d, plan.slot_pos.data_ptr(), recv_w.data_ptr(),
-                  R_tok, k, partial.data_ptr(), _lib.FK_BF16, st)
-        back = ex.all_to_all(partial)
+        if px is not None:
+            _lib.call("fk_ep_peer_combine_put", y.data_ptr(), d, plan.slot_pos.data_ptr(), recv_w_p,
+                      T, N, ex.rank, k, None, px.table("to_source"), None, px.table("flags"),
+                      px.PHASE_FWD_COMBINE, px.ctl.data_ptr(), _lib.FK_BF16, st)
+            px.wait(px.PHASE_FWD_COMBINE, st)
+            back_p = px.local("to_source")
+        else:
+            partial = torch.empty(R_tok, d, **bf)
+            _lib.call("fk_moe_combine", y.data_ptr(), d, plan.slot_pos.data_ptr(), recv_w_p,
+                      R_tok, k, partial.data_ptr(), _lib.FK_BF16, st)
+            back = ex.all_to_all(partial)
+            back_p = back.data_ptr()
         out = torch.empty(T, d, **bf)
-        _lib.call("fk_ep_unpack_sum", back.data_ptr(), d, src_pos.data_ptr(), T, N, out.data_ptr(),
+        _lib.call("fk_ep_unpack_sum", back_p, d, src_pos.data_ptr(), T, N, out.data_ptr(),
                   _lib.FK_BF16, st)
         ctx.save_for_backward(xs, h1, act, y, idx, src_pos, send_token)
         ctx.plan = plan
@@ -155,18 +247,27 @@ class _EPMoEFn(torch.autograd.Function):
         eptr = plan.err.data_ptr()
         bf = dict(dtype=torch.bfloat16, device=dev)
         dout = dout.to(torch.bfloat16).contiguous()
-        send_d = torch.empty(R_tok, d, **bf)
-        _lib.call("fk_ep_pack", dout.data_ptr(), d, send_token.data_ptr(), R_tok, send_d.data_ptr(),
-                  _lib.FK_BF16, st)
-        recv_d = ex.all_to_all(send_d)
+        px = layer._peer(T, d, k, dev) if layer.transport == "peer" else None
+        if px is not None:
+            _lib.call("fk_ep_peer_put_rows", dout.data_ptr(), d, send_token.data_ptr(), T, N,
+                      ex.rank, None, None, k, px.table("to_expert"), None, None,
+                      px.table("flags"), px.PHASE_BWD_DISPATCH, px.ctl.data_ptr(),
+                      _lib.FK_BF16, st)
+            px.wait(px.PHASE_BWD_DISPATCH, st)
+            recv_d_p = px.local("to_expert")
+        else:
+            send_d = torch.empty(R_tok, d, **bf)
+            _lib.call("fk_ep_pack", dout.data_ptr(), d, send_token.data_ptr(), R_tok,
+                      send_d.data_ptr(), _lib.FK_BF16, st)
+            recv_d = ex.all_to_all(send_d)
+            recv_d_p = recv_d.data_ptr()
         dy = torch.empty(R, d, **bf)
         dw_recv = torch.zeros(R_tok, k, dtype=torch.float32, device=dev)
         dh1 = torch.empty(R, 2 * H, **bf)
         dxs = torch.empty(R, d, **bf)
         dw13 = torch.empty(El, 2 * H, d, **bf)
         dw2 = torch.empty(El, d, H, **bf)
-        dx_part = torch.empty(R_tok, d, **bf)
-        _lib.call("fk_moe_combine_bwd", recv_d.data_ptr(), y.data_ptr(), d,
+        _lib.call("fk_moe_combine_bwd", recv_d_p, y.data_ptr(), d,
                   plan.sorted_assign.data_ptr(), plan.sorted_w.data_ptr(), k,
                   plan.n_mblk.data_ptr(), R, dy.data_ptr(), dw_recv.data_ptr(), _lib.FK_BF16, st)
         _lib.call("fk_moe_gemm_down_dgrad", dy.data_ptr(), R, d, layer.w2.data_ptr(), H, El,
@@ -174,22 +275,34 @@ class _EPMoEFn(torch.autograd.Function):
                   dh1.data_ptr(), eptr + 4, st)
         _lib.call("fk_moe_gemm_up_dgrad", dh1.data_ptr(), R, H, layer.w13.data_ptr(), d, El,
                   plan.tile_expert.data_ptr(), plan.n_mblk.data_ptr(), dxs.data_ptr(), eptr + 4, st)
-        _lib.call("fk_moe_combine", dxs.data_ptr(), d, plan.slot_pos.data_ptr(), None, R_tok, k,
-                  dx_part.data_ptr(), _lib.FK_BF16, st)
-        # input-gradient and routing-gradient exchange overlap the weight-gradient GEMMs
-        back_dx, w1 = ex.all_to_all(dx_part, async_op=True)
-        back_dw, w2 = ex.all_to_all(dw_recv, async_op=True)
+        # The input-gradient and routing-gradient exchange overlaps the weight-gradient GEMMs.
+        if px is not None:
+            _lib.call("fk_ep_peer_combine_put", dxs.data_ptr(), d, plan.slot_pos.data_ptr(), None,
+                      T, N, ex.rank, k, dw_recv.data_ptr(), px.table("to_source"),
+                      px.table("dw"), px.table("flags"), px.PHASE_BWD_COMBINE,
+                      px.ctl.data_ptr(), _lib.FK_BF16, st)
+        else:
+            dx_part = torch.empty(R_tok, d, **bf)
+            _lib.call("fk_moe_combine", dxs.data_ptr(), d, plan.slot_pos.data_ptr(), None, R_tok,
+                      k, dx_part.data_ptr(), _lib.FK_BF16, st)
+            back_dx, w1 = ex.all_to_all(dx_part, async_op=True)
+            back_dw, w2 = ex.all_to_all(dw_recv, async_op=True)
         _lib.call("fk_moe_gemm_wgrad", dy.data_ptr(), d, act.data_ptr(), H, R,
                   plan.seg_start.data_ptr(), El, dw2.data_ptr(), eptr + 4, st)
         _lib.call("fk_moe_gemm_wgrad", dh1.data_ptr(), 2 * H, xs.data_ptr(), d, R,
                   plan.seg_start.data_ptr(), El, dw13.data_ptr(), eptr + 4, st)
-        w1.wait()
-        w2.wait()
+        if px is not None:
+            px.wait(px.PHASE_BWD_COMBINE, st)
+            back_dx_p, back_dw_p = px.local("to_source"), px.local("dw")
+        else:
+            w1.wait()
+            w2.wait()
+            back_dx_p, back_dw_p = back_dx.data_ptr(), back_dw.data_ptr()
         dx = torch.empty(T, d, **bf)
-        _lib.call("fk_ep_unpack_sum", back_dx.data_ptr(), d, src_pos.data_ptr(), T, N,
+        _lib.call("fk_ep_unpack_sum", back_dx_p, d, src_pos.data_ptr(), T, N,
                   dx.data_ptr(), _lib.FK_BF16, st)
         dw = torch.empty(T, k, dtype=torch.float32, device=dev)
-        _lib.call("fk_ep_unpack_dw", back_dw.data_ptr(), idx.data_ptr(),
+        _lib.call("fk_ep_unpack_dw", back_dw_p, idx.data_ptr(),
                   layer.expert_rank.data_ptr(), src_pos.data_ptr(), T, k, N, E, dw.data_ptr(), st)
         grads = []
         for e in range(El):
@@ -204,9 +317,12 @@ class ExpertParallelMoEMLP(nn.Module):
     construct the layer with the same placement."""
 
     def __init__(self, dim: int, hidden_dim: int, n_experts: int, k: int = 2, group=None,
-                 placement=None, router_version: str = "v2"):
+                 placement=None, router_version: str = "v2", transport: str = "peer"):
         super().__init__()
         assert router_version == "v2"
+        assert transport in ("peer", "nccl")
+        self.transport = transport
+        self._peer_ex = None
         self.dim, self.hidden_dim, self.n_experts, self.k = dim, hidden_dim, n_experts, k
         self.exchange = Exchange(group)
         N, r = self.exchange.world, self.exchange.rank
@@ -260,6 +376,30 @@ class ExpertParallelMoEMLP(nn.Module):
             self.w13[i, :self.hidden_dim].copy_(w_gate[e])
             self.w13[i, self.hidden_dim:].copy_(w_up[e])
             self.w2[i].copy_(w_down[e])
+
+    def _peer(self, n_tokens: int, dim: int, k: int, device) -> PeerExchange:
+        """The peer-memory exchange for T = n_tokens per rank (created on first use; every
+        rank must call with the same T)."""
+        px = self._peer_ex
+        if px is not None and px.key == (n_tokens, dim, k):
+            return px
+        if torch.cuda.is_current_stream_capturing():
+            raise RuntimeError("ExpertParallelMoEMLP: run one step eagerly before capturing "
+                               "a CUDA graph (the peer exchange is set up on first use)")
+        if px is not None:
+            px.close()
+        self._peer_ex = PeerExchange(self.exchange.group, n_tokens, dim, k, device)
+        return self._peer_ex
+
+    def close(self) -> None:
+        """Collective: release the peer-memory exchange (before destroy_process_group)."""
+        if self._peer_ex is not None:
+            self._peer_ex.close()
+            self._peer_ex = None
+
+    def peer_error(self) -> int:
+        """Device error flag of the peer transport (16 + phase after a wait timed out)."""
+        return 0 if self._peer_ex is None else int(self._peer_ex.err.item())
 
     def allreduce_router_grad(self):
         g = self.router.weight.grad

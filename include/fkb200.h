@@ -242,6 +242,40 @@ FK_API int fk_ep_unpack_dw(const float* back_dw, const int64_t* idx, const int* 
                            const int* src_pos, int64_t n_tokens, int k, int n_ranks,
                            int n_experts, float* dw, void* stream);
 
+/* ---------------------------------------------------------------- EP over peer memory
+ * No counterpart in the reference (it has no distributed code).  The NVLink transport of
+ * the expert-parallel layer: each rank owns one exchange region (fk_ipc_alloc, exported by
+ * CUDA IPC, opened by the other ranks with fk_ipc_open) with the fixed-capacity layout of
+ * fk_ep_plan; put kernels store rows directly into the peers' regions and publish a
+ * per-phase sequence number into every rank's flags; fk_ep_peer_wait waits (at most
+ * timeout_ms; err_flag = 16 + phase on timeout) until every rank has published the phase.
+ * *_bases are DEVICE arrays of n_ranks pointers (this rank's own region included);
+ * flag_bases[d] points at rank d's flags [4][n_ranks]; ctl is this rank's 24-word
+ * control block (zeroed once).
+ * fk_ep_peer_put_rows: row r < n_ranks*T with token send_token[r] >= 0 is copied to
+ *   row_bases[r / T] row (my_rank*T + r % T); with send_e, the k slot entries of every
+ *   row go to e_bases / w_bases at the same row.  Replaces fk_ep_pack + all-to-all.
+ * fk_ep_peer_combine_put: for every received row j with a local slot, the weighted sum
+ *   of its slots' y rows (w null: unweighted) goes to row_bases[j / T] row
+ *   (my_rank*T + j % T), and with dw_rows its k entries to dw_bases at the same row.
+ *   Replaces fk_moe_combine + all-to-all on the expert side. */
+FK_API int fk_ipc_alloc(size_t bytes, void** ptr, void* handle64);
+FK_API int fk_ipc_open(const void* handle64, void** ptr);
+FK_API int fk_ipc_close(void* ptr);
+FK_API int fk_ipc_free(void* ptr);
+FK_API int fk_ep_peer_put_rows(const void* x, int dim, const int* send_token, int64_t n_tokens,
+                               int n_ranks, int my_rank, const int* send_e, const float* send_w,
+                               int k, void* const* row_bases, void* const* e_bases,
+                               void* const* w_bases, unsigned* const* flag_bases, int phase,
+                               unsigned* ctl, int dtype, void* stream);
+FK_API int fk_ep_peer_combine_put(const void* y, int dim, const int* slot_pos, const float* w,
+                                  int64_t n_tokens, int n_ranks, int my_rank, int k,
+                                  const float* dw_rows, void* const* row_bases,
+                                  void* const* dw_bases, unsigned* const* flag_bases, int phase,
+                                  unsigned* ctl, int dtype, void* stream);
+FK_API int fk_ep_peer_wait(const unsigned* flags, int n_ranks, int phase, unsigned* ctl,
+                           int timeout_ms, int* err_flag, void* stream);
+
 /* ---------------------------------------------------------------- bitonic utilities
  * int32 row sorts in shared memory, one CTA per row, rows of at most 2048 keys.
  * fk_bitonic_sort_i32: each row ascending (replaces _bitonic_sort_ascending_kernel,

@@ -10,7 +10,7 @@ import pytest
 import torch
 import torch.distributed as dist
 
-from fusedkernels_b200 import _lib
+from fusedkernels_b200 import _lib, fused_moe_route_v2
 from fusedkernels_b200.moe_ep import ExpertParallelMoEMLP, lpt_placement
 from fusedkernels_b200.moe_layer_sorted import FusedMoEMLPSorted
 from oracle import route_oracle
@@ -96,7 +96,8 @@ def _single_gpu(D, H, E, k, wts, x, dout):
     return layer, out.detach(), xg.grad
 
 
-def test_ep_layer_one_rank_matches_single_gpu_bitwise():
+@pytest.mark.parametrize("transport", ["peer", "nccl"])
+def test_ep_layer_one_rank_matches_single_gpu_bitwise(transport):
     D, H, E, k, T = 256, 256, 16, 4, 512
     wts = _make_weights(D, H, E, 1)
     G = gen(2)
@@ -106,12 +107,15 @@ def test_ep_layer_one_rank_matches_single_gpu_bitwise():
     store = dist.TCPStore("127.0.0.1", _free_port(), 1, True)
     dist.init_process_group("nccl", store=store, rank=0, world_size=1)
     try:
-        ep = ExpertParallelMoEMLP(D, H, E, k).to(DEV).bfloat16()
+        ep = ExpertParallelMoEMLP(D, H, E, k, transport=transport).to(DEV).bfloat16()
         ep.load_from_full(*(t.bfloat16().to(DEV) for t in wts))
-        xg = x.clone().requires_grad_(True)
-        out = ep(xg)
-        out.backward(dout)
+        for _ in range(2):  # the second step reuses the exchange regions
+            ep.zero_grad(set_to_none=True)
+            xg = x.clone().requires_grad_(True)
+            out = ep(xg)
+            out.backward(dout)
         torch.cuda.synchronize()
+        assert ep.peer_error() == 0
         assert torch.equal(out, ref_out)
         assert torch.equal(xg.grad, ref_dx)
         assert torch.equal(ep.router.weight.grad, ref_layer.router.weight.grad)
@@ -119,11 +123,69 @@ def test_ep_layer_one_rank_matches_single_gpu_bitwise():
             a, b = ep.experts[str(e)], ref_layer.experts[e]
             assert torch.equal(a.w_gate.weight.grad, b.w_gate.weight.grad)
             assert torch.equal(a.w_down.weight.grad, b.w_down.weight.grad)
+        ep.close()
     finally:
         dist.destroy_process_group()
 
 
-def _ep_worker(rank, world, port, q):
+def test_ep_peer_layer_cuda_graph_replay():
+    """The peer transport keeps its sequence numbers on the device: a captured step
+    replays correctly (one rank)."""
+    D, H, E, k, T = 256, 256, 16, 4, 512
+    wts = _make_weights(D, H, E, 1)
+    G = gen(4)
+    x = torch.randn(T, D, generator=G).bfloat16().to(DEV)
+    dout = torch.randn(T, D, generator=G).bfloat16().to(DEV)
+    store = dist.TCPStore("127.0.0.1", _free_port(), 1, True)
+    dist.init_process_group("nccl", store=store, rank=0, world_size=1)
+    try:
+        ep = ExpertParallelMoEMLP(D, H, E, k, transport="peer").to(DEV).bfloat16()
+        ep.load_from_full(*(t.bfloat16().to(DEV) for t in wts))
+        xg = x.clone().requires_grad_(True)
+
+        def step():
+            xg.grad = None
+            out = ep(xg)
+            out.backward(dout)
+            return out
+
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            eager = step().clone()
+            eager_dx = xg.grad.clone()
+        torch.cuda.current_stream().wait_stream(side)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            out = step()
+        for _ in range(3):
+            g.replay()
+        torch.cuda.synchronize()
+        assert ep.peer_error() == 0
+        assert torch.equal(out, eager)
+        assert torch.equal(xg.grad, eager_dx)
+        del g
+        ep.close()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_ep_peer_wait_times_out_and_reports():
+    """A phase that no rank publishes: the wait gives up after its bound (0.5 s), records
+    16 + phase and leaves the context usable."""
+    flags = torch.zeros(4, dtype=torch.int32, device=DEV)
+    ctl = torch.zeros(24, dtype=torch.int32, device=DEV)
+    err = torch.zeros(1, dtype=torch.int32, device=DEV)
+    st = torch.cuda.current_stream().cuda_stream
+    _lib.call("fk_ep_peer_wait", flags.data_ptr(), 1, 2, ctl.data_ptr(), 500, err.data_ptr(), st)
+    torch.cuda.synchronize()
+    assert err.item() == 18
+    assert ctl[16 + 2].item() == 1  # the expected sequence number moved on
+    assert (torch.ones(4, device=DEV) * 2).sum().item() == 8.0
+
+
+def _ep_worker(rank, world, port, q, transport="peer"):
     import sys
     root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
     sys.path.insert(0, root)
@@ -140,28 +202,35 @@ def _ep_worker(rank, world, port, q):
         G = torch.Generator().manual_seed(3)
         x_all = torch.randn(world * T, D, generator=G).bfloat16()
         d_all = torch.randn(world * T, D, generator=G).bfloat16()
-        ep = ExpertParallelMoEMLP(D, H, E, k, placement=lpt_placement([1.0] * E, world)).to(dev).bfloat16()
+        ep = ExpertParallelMoEMLP(D, H, E, k, placement=lpt_placement([1.0] * E, world),
+                                  transport=transport).to(dev).bfloat16()
         ep.load_from_full(*(t.bfloat16().to(dev) for t in wts))
         x = x_all[rank * T:(rank + 1) * T].to(dev).requires_grad_(True)
         out = ep(x)
         out.backward(d_all[rank * T:(rank + 1) * T].to(dev))
+        with torch.no_grad():
+            _, idx = fused_moe_route_v2(ep.router(x.detach()), k)
         torch.cuda.synchronize()
-        q.put((rank, out.detach().float().cpu(), x.grad.detach().float().cpu()))
+        assert ep.peer_error() == 0, f"peer wait timed out: {ep.peer_error()}"
+        ep.close()
+        q.put((rank, out.detach().float().cpu(), x.grad.detach().float().cpu(), idx.cpu()))
     except Exception as exc:
-        q.put((rank, repr(exc), None))
+        q.put((rank, repr(exc), None, None))
     finally:
         if dist.is_initialized():
             dist.destroy_process_group()
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_ep_layer_two_ranks_matches_single_gpu():
+@pytest.mark.parametrize("transport", ["peer", "nccl"])
+def test_ep_layer_two_ranks_matches_single_gpu(transport):
     import torch.multiprocessing as mp
     D, H, E, k, T, world = 256, 256, 16, 4, 256, 2
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_ep_worker, args=(r, world, port, q)) for r in range(world)]
+    procs = [ctx.Process(target=_ep_worker, args=(r, world, port, q, transport))
+             for r in range(world)]
     for p in procs:
         p.start()
     res = sorted([q.get(timeout=180) for _ in procs], key=lambda r: r[0])
@@ -173,10 +242,16 @@ def test_ep_layer_two_ranks_matches_single_gpu():
     G = torch.Generator().manual_seed(3)
     x_all = torch.randn(world * T, D, generator=G).bfloat16().to(DEV)
     d_all = torch.randn(world * T, D, generator=G).bfloat16().to(DEV)
-    _, ref_out, ref_dx = _single_gpu(D, H, E, k, wts, x_all, d_all)
-    out = torch.cat([r[1] for r in res])
-    dx = torch.cat([r[2] for r in res])
-    scale = ref_out.abs().max().item()
-    assert (out - ref_out.float().cpu()).abs().max().item() <= 2e-2 * scale
-    scale = ref_dx.abs().max().item()
-    assert (dx - ref_dx.float().cpu()).abs().max().item() <= 2e-2 * scale
+    # Tokens are independent, so the single-GPU layer runs on each rank's T tokens: the
+    # router GEMM then has the same shape on both sides and the bf16 logits (and with them
+    # the expert selection, which a 1-ulp difference on a near-tie would flip) are equal.
+    for r in res:
+        sl = slice(r[0] * T, (r[0] + 1) * T)
+        layer, ref_out, ref_dx = _single_gpu(D, H, E, k, wts, x_all[sl], d_all[sl])
+        with torch.no_grad():
+            _, ref_idx = fused_moe_route_v2(layer.router(x_all[sl]), k)
+        assert torch.equal(r[3], ref_idx.cpu()), f"rank {r[0]}: routing differs"
+        scale = ref_out.abs().max().item()
+        assert (r[1] - ref_out.float().cpu()).abs().max().item() <= 2e-2 * scale, f"rank {r[0]} out"
+        scale = ref_dx.abs().max().item()
+        assert (r[2] - ref_dx.float().cpu()).abs().max().item() <= 2e-2 * scale, f"rank {r[0]} dx"

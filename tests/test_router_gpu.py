@@ -55,6 +55,13 @@ def test_router_16bit_ties_bit_exact(E, k, dtype):
     assert idx.shape == (4096, k)
 
 
+@pytest.mark.parametrize("n", [1, 3, 1001])
+@pytest.mark.parametrize("E,k", [(8, 1), (9, 2), (64, 2), (128, 8), (256, 4)])
+def test_router_ragged_row_counts(n, E, k):
+    """Row counts that leave part of the last warp's rows empty."""
+    check(torch.randn(n, E, generator=gen(n * 7 + E + k)), k)
+
+
 def test_router_integer_logits_many_ties():
     logits = torch.randint(-2, 3, (2048, 64), generator=gen(12)).float()
     check(logits, 8)
