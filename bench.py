@@ -901,15 +901,23 @@ def run_breakdown(args, reps=5):
     """Per-call device time of one step: every C-ABI call of the step is bracketed by CUDA
     events (eager launches), averaged over `reps` steps."""
     import collections
-    from fusedkernels_b200 import _lib
+    from fusedkernels_b200 import _lib, moe_ep
+    world = int(os.environ.get("WORLD_SIZE", "1"))
     dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
     torch.cuda.set_device(dev)
+    if world > 1:
+        import datetime
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                             device_id=dev)
     wl = make_workload(args)
+    if args.workload == "moe":
+        wl.ep_transport = args.ep_transport
     wl.setup(dev)
     for _ in range(max(args.warmup, 3)):
         wl.step()
     torch.cuda.synchronize()
     orig = _lib.call
+    orig_a2a = moe_ep.Exchange.all_to_all
     rec = []
 
     def timed(name, *a):
@@ -919,7 +927,16 @@ def run_breakdown(args, reps=5):
         s1.record()
         rec.append((name, s0, s1))
 
+    def timed_a2a(self, send, async_op=False):
+        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s0.record()
+        r = orig_a2a(self, send, async_op)
+        s1.record()
+        rec.append(("nccl all_to_all" + (" (async launch)" if async_op else ""), s0, s1))
+        return r
+
     _lib.call = timed
+    moe_ep.Exchange.all_to_all = timed_a2a
     tot, cnt, step_ms = collections.defaultdict(float), collections.Counter(), 0.0
     try:
         for _ in range(reps):
@@ -935,11 +952,20 @@ def run_breakdown(args, reps=5):
                 cnt[n] += 1
     finally:
         _lib.call = orig
-    print(f"| call | launches | ms / step |\n|---|---|---|")
-    for n, t in sorted(tot.items(), key=lambda kv: -kv[1]):
-        print(f"| {n} | {cnt[n] // reps} | {t:.3f} |")
-    print(f"| sum of C-ABI calls | | {sum(tot.values()):.3f} |")
-    print(f"| whole eager step | | {step_ms:.3f} |")
+        moe_ep.Exchange.all_to_all = orig_a2a
+    if int(os.environ.get("RANK", "0")) == 0:
+        print(f"| call | launches | ms / step |\n|---|---|---|")
+        for n, t in sorted(tot.items(), key=lambda kv: -kv[1]):
+            print(f"| {n} | {cnt[n] // reps} | {t:.3f} |")
+        print(f"| sum of timed calls | | {sum(tot.values()):.3f} |")
+        print(f"| whole eager step | | {step_ms:.3f} |")
+    if world > 1:
+        torch.cuda.synchronize()
+        layer = getattr(wl, "layer", None)
+        if hasattr(layer, "close"):
+            layer.close()
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
 
 
 def wl_setup_host(wl):

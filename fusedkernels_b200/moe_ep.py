@@ -58,6 +58,17 @@ def round_robin_placement(n_experts: int, n_ranks: int) -> list[int]:
     return [e % n_ranks for e in range(n_experts)]
 
 
+def owner_local_index(placement, n_ranks: int) -> list[int]:
+    """For every expert, its position among the experts of the rank that owns it (the
+    order of that rank's stacked weights: ascending global id)."""
+    seen = [0] * n_ranks
+    out = []
+    for r in placement:
+        out.append(seen[r])
+        seen[r] += 1
+    return out
+
+
 class Exchange:
     """Fixed-capacity all-to-all of [n_ranks * cap, ...] buffers over a process group
     (the NCCL transport)."""
@@ -330,13 +341,13 @@ class ExpertParallelMoEMLP(nn.Module):
         assert len(placement) == n_experts and all(0 <= p < N for p in placement)
         self.placement = placement
         self.local_ids = [e for e in range(n_experts) if placement[e] == r]
-        local_of = {e: i for i, e in enumerate(self.local_ids)}
         self.router = nn.Linear(dim, n_experts, bias=False)
         self.experts = nn.ModuleDict({str(e): Expert(dim, hidden_dim) for e in self.local_ids})
         self.register_buffer("expert_rank", torch.tensor(placement, dtype=torch.int32), persistent=False)
-        self.register_buffer("expert_local",
-                             torch.tensor([local_of.get(e, -1) for e in range(n_experts)],
-                                          dtype=torch.int32), persistent=False)
+        # index of every expert inside its OWNER's stacked weights (the destination rank of
+        # a slot looks its expert up in this table when the slot is planned)
+        self.register_buffer("expert_local", torch.tensor(owner_local_index(placement, N),
+                                                          dtype=torch.int32), persistent=False)
         self._restack()
 
     def _expert_params(self):

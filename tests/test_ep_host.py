@@ -31,6 +31,19 @@ def test_lpt_placement_balances_zipf_load():
     assert lpt == lpt_placement(load.tolist(), N)  # deterministic
 
 
+def test_owner_local_index_matches_per_rank_order():
+    """The destination rank of a slot stacks its experts in ascending global id; the
+    planning table must give every expert's index there, for remote experts too."""
+    from fusedkernels_b200.moe_ep import owner_local_index
+    G = torch.Generator().manual_seed(5)
+    for E, N in [(8, 2), (128, 8), (64, 4)]:
+        pl = lpt_placement(torch.rand(E, generator=G).tolist(), N)
+        table = owner_local_index(pl, N)
+        for r in range(N):
+            ids = [e for e in range(E) if pl[e] == r]
+            assert [table[e] for e in ids] == list(range(len(ids)))
+
+
 def test_lpt_placement_rejects_uneven():
     with pytest.raises(ValueError):
         lpt_placement([1.0] * 10, 4)
