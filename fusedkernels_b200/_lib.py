@@ -47,7 +47,9 @@ SIGNATURES: dict[str, list] = {
     "fk_moe_gemm_wgrad": [_vp, _i32, _vp, _i32, _i64, _vp, _i32, _vp, _vp, _vp],
     "fk_moe_route_meta_skip": [_vp, _vp, _i64, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
                                _i64, _vp, _sz, _vp, _vp],
-    "fk_ep_plan": [_vp, _vp, _i64, _i32, _vp, _vp, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp],
+    "fk_ep_plan_workspace_size": [_i64, _i32, C.POINTER(_sz)],
+    "fk_ep_plan": [_vp, _vp, _i64, _i32, _vp, _vp, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _sz,
+                   _vp, _vp],
     "fk_ep_pack": [_vp, _i32, _vp, _i64, _vp, _i32, _vp],
     "fk_ep_unpack_sum": [_vp, _i32, _vp, _i64, _i32, _vp, _i32, _vp],
     "fk_ep_unpack_dw": [_vp, _vp, _vp, _vp, _i64, _i32, _i32, _i32, _vp, _vp],
@@ -130,6 +132,13 @@ def rmsnorm_bwd_workspace_bytes(rows: int, cols: int, device: torch.device) -> i
                   "fk_rmsnorm_bwd_workspace_size")
         v = _ws_cache[key] = out.value
     return v
+
+
+def ep_plan_workspace_bytes(n_tokens: int, n_ranks: int) -> int:
+    out = C.c_size_t(0)
+    check(load().fk_ep_plan_workspace_size(n_tokens, n_ranks, C.byref(out)),
+          "fk_ep_plan_workspace_size")
+    return out.value
 
 
 _cap_cache: dict = {}

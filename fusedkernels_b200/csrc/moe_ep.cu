@@ -16,71 +16,103 @@
 namespace fk {
 namespace {
 
-constexpr int kPlanThreads = 1024;
+constexpr int kPlanThreads = 256;  // tokens per planning CTA
 
-// One CTA per destination rank d: stable compaction (by token index) of the tokens that
-// have a slot on d.
-__global__ void __launch_bounds__(kPlanThreads) ep_plan_kernel(
+__device__ __forceinline__ uint32_t lanes_below() {
+  uint32_t m;
+  asm("mov.u32 %0, %%lanemask_lt;" : "=r"(m));
+  return m;
+}
+
+// Bit d of the result: token t has at least one slot on rank d.
+__device__ __forceinline__ uint32_t dest_mask(const int64_t* __restrict__ idx, int64_t t, int k,
+                                              const int* __restrict__ expert_rank, int E,
+                                              int* __restrict__ err) {
+  uint32_t m = 0;
+  for (int j = 0; j < k; ++j) {
+    const int64_t e = idx[t * k + j];
+    if (e < 0 || e >= E) {
+      if (err) atomicExch(err, 1);
+      continue;
+    }
+    m |= 1u << expert_rank[e];
+  }
+  return m;
+}
+
+// Pass 1: per chunk of kPlanThreads tokens, how many have a slot on each rank.
+__global__ void __launch_bounds__(kPlanThreads) ep_plan_count_kernel(
+    const int64_t* __restrict__ idx, int64_t T, int k, const int* __restrict__ expert_rank, int E,
+    int n_ranks, int* __restrict__ chunk_count, int* __restrict__ err) {
+  const int64_t t = (int64_t)blockIdx.x * kPlanThreads + threadIdx.x;
+  const uint32_t m = t < T ? dest_mask(idx, t, k, expert_rank, E, err) : 0u;
+  for (int d = 0; d < n_ranks; ++d) {
+    const int c = __syncthreads_count((m >> d) & 1u);
+    if (threadIdx.x == 0) chunk_count[(int64_t)blockIdx.x * n_ranks + d] = c;
+  }
+}
+
+// Pass 2: stable position of every token in every destination's list (counts of the
+// earlier chunks + rank inside this chunk), the send lists, and -1 rows past every
+// destination's count (rows c*kPlanThreads + tid of each destination).
+__global__ void __launch_bounds__(kPlanThreads) ep_plan_fill_kernel(
     const int64_t* __restrict__ idx, const float* __restrict__ w, int64_t T, int k,
     const int* __restrict__ expert_rank, const int* __restrict__ expert_local, int E,
-    int n_ranks, int* __restrict__ send_token, int* __restrict__ send_e,
-    float* __restrict__ send_w, int* __restrict__ src_pos, int* __restrict__ send_count,
-    int* __restrict__ err) {
-  __shared__ int warp_tot[32];
-  __shared__ int base_s;
-  const int d = blockIdx.x;
+    int n_ranks, const int* __restrict__ chunk_count, int n_chunks, int* __restrict__ send_token,
+    int* __restrict__ send_e, float* __restrict__ send_w, int* __restrict__ src_pos,
+    int* __restrict__ send_count) {
+  constexpr int kWarps = kPlanThreads / 32;
+  __shared__ int base[32], total[32];
+  __shared__ uint32_t wbal[kWarps][32];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  if (tid == 0) base_s = 0;
+  const int c = blockIdx.x;
+  if (tid < n_ranks) {
+    int b = 0, tot = 0;
+    for (int i = 0; i < n_chunks; ++i) {
+      const int v = chunk_count[(int64_t)i * n_ranks + tid];
+      if (i < c) b += v;
+      tot += v;
+    }
+    base[tid] = b;
+    total[tid] = tot;
+    if (c == 0) send_count[tid] = tot;
+  }
+  const int64_t t = (int64_t)c * kPlanThreads + tid;
+  const uint32_t m = t < T ? dest_mask(idx, t, k, expert_rank, E, nullptr) : 0u;
+  for (int d = 0; d < n_ranks; ++d) {
+    const uint32_t bal = __ballot_sync(0xffffffffu, (m >> d) & 1u);
+    if (lane == 0) wbal[warp][d] = bal;
+  }
   __syncthreads();
-  for (int64_t t0 = 0; t0 < T; t0 += kPlanThreads) {
-    const int64_t t = t0 + tid;
-    bool has = false;
-    if (t < T) {
+  if (t < T) {
+    for (int d = 0; d < n_ranks; ++d) {
+      if (!((m >> d) & 1u)) {
+        src_pos[t * n_ranks + d] = -1;
+        continue;
+      }
+      int pos = base[d] + __popc(wbal[warp][d] & lanes_below());
+      for (int i = 0; i < warp; ++i) pos += __popc(wbal[i][d]);
+      src_pos[t * n_ranks + d] = pos;
+      const int64_t r = (int64_t)d * T + pos;
+      send_token[r] = (int)t;
       for (int j = 0; j < k; ++j) {
         const int64_t e = idx[t * k + j];
-        if (e < 0 || e >= E) {
-          atomicExch(err, 1);
-          continue;
-        }
-        has |= expert_rank[e] == d;
+        const bool mine = e >= 0 && e < E && expert_rank[e] == d;
+        send_e[r * k + j] = mine ? expert_local[e] : -1;
+        send_w[r * k + j] = w[t * k + j];
       }
     }
-    const uint32_t bal = __ballot_sync(0xffffffffu, has);
-    if (lane == 0) warp_tot[warp] = __popc(bal);
-    __syncthreads();
-    int before = 0;
-    for (int i = 0; i < warp; ++i) before += warp_tot[i];
-    const int base = base_s;
-    const int pos = base + before + __popc(bal & ((1u << lane) - 1u));
-    if (t < T) {
-      src_pos[t * n_ranks + d] = has ? pos : -1;
-      if (has) {
-        const int64_t r = (int64_t)d * T + pos;
-        send_token[r] = (int)t;
-        for (int j = 0; j < k; ++j) {
-          const int64_t e = idx[t * k + j];
-          const bool mine = e >= 0 && e < E && expert_rank[e] == d;
-          send_e[r * k + j] = mine ? expert_local[e] : -1;
-          send_w[r * k + j] = w[t * k + j];
-        }
-      }
-    }
-    __syncthreads();
-    if (tid == 0) {
-      int tot = 0;
-      for (int i = 0; i < kPlanThreads / 32; ++i) tot += warp_tot[i];
-      base_s = base + tot;
-    }
-    __syncthreads();
   }
-  const int count = base_s;
-  if (tid == 0) send_count[d] = count;
-  // Rows past the count carry no slot for the receiver.
-  for (int64_t r = count + tid; r < T; r += kPlanThreads) {
-    send_token[(int64_t)d * T + r] = -1;
-    for (int j = 0; j < k; ++j) {
-      send_e[((int64_t)d * T + r) * k + j] = -1;
-      send_w[((int64_t)d * T + r) * k + j] = 0.f;
+  const int64_t p = (int64_t)c * kPlanThreads + tid;
+  if (p < T) {
+    for (int d = 0; d < n_ranks; ++d) {
+      if (p < total[d]) continue;
+      const int64_t r = (int64_t)d * T + p;
+      send_token[r] = -1;
+      for (int j = 0; j < k; ++j) {
+        send_e[r * k + j] = -1;
+        send_w[r * k + j] = 0.f;
+      }
     }
   }
 }
@@ -166,19 +198,41 @@ inline int rows_grid(int64_t rows) {
 }  // namespace
 }  // namespace fk
 
+extern "C" int fk_ep_plan_workspace_size(int64_t n_tokens, int n_ranks, size_t* bytes) {
+  FK_CHECK_ARG(n_tokens >= 0 && n_ranks >= 1 && n_ranks <= 32 && bytes,
+               "fk_ep_plan_workspace_size: bad arguments");
+  const int64_t chunks = (n_tokens + fk::kPlanThreads - 1) / fk::kPlanThreads;
+  *bytes = (size_t)(chunks < 1 ? 1 : chunks) * n_ranks * sizeof(int);
+  return FK_OK;
+}
+
 extern "C" int fk_ep_plan(const int64_t* idx, const float* w, int64_t n_tokens, int k,
                           const int* expert_rank, const int* expert_local, int n_experts,
                           int n_ranks, int* send_token, int* send_e, float* send_w,
-                          int* src_pos, int* send_count, int* err_flag, void* stream) {
-  FK_CHECK_ARG(n_tokens >= 0 && k >= 1 && n_ranks >= 1 && n_experts >= 1, "fk_ep_plan: bad sizes");
+                          int* src_pos, int* send_count, void* workspace, size_t ws_bytes,
+                          int* err_flag, void* stream) {
+  FK_CHECK_ARG(n_tokens >= 0 && k >= 1 && n_ranks >= 1 && n_ranks <= 32 && n_experts >= 1,
+               "fk_ep_plan: bad sizes (1 <= n_ranks <= 32)");
   FK_CHECK_ARG(expert_rank && expert_local && send_token && send_e && send_w && src_pos &&
-                   send_count && err_flag && (n_tokens == 0 || (idx && w)),
+                   send_count && err_flag && workspace && (n_tokens == 0 || (idx && w)),
                "fk_ep_plan: null pointer");
+  size_t need = 0;
+  fk_ep_plan_workspace_size(n_tokens, n_ranks, &need);
+  if (ws_bytes < need)
+    return fk::fail(FK_ERR_WORKSPACE, "fk_ep_plan: workspace %zu < %zu bytes", ws_bytes, need);
   cudaStream_t st = fk::as_stream(stream);
   cudaMemsetAsync(err_flag, 0, sizeof(int), st);
-  fk::ep_plan_kernel<<<n_ranks, fk::kPlanThreads, 0, st>>>(
-      idx, w, n_tokens, k, expert_rank, expert_local, n_experts, n_ranks, send_token, send_e,
-      send_w, src_pos, send_count, err_flag);
+  const int chunks = (int)((n_tokens + fk::kPlanThreads - 1) / fk::kPlanThreads);
+  int* cc = static_cast<int*>(workspace);
+  if (chunks == 0) {
+    cudaMemsetAsync(send_count, 0, n_ranks * sizeof(int), st);
+    return fk::launch_status("fk_ep_plan");
+  }
+  fk::ep_plan_count_kernel<<<chunks, fk::kPlanThreads, 0, st>>>(idx, n_tokens, k, expert_rank,
+                                                               n_experts, n_ranks, cc, err_flag);
+  fk::ep_plan_fill_kernel<<<chunks, fk::kPlanThreads, 0, st>>>(
+      idx, w, n_tokens, k, expert_rank, expert_local, n_experts, n_ranks, cc, chunks, send_token,
+      send_e, send_w, src_pos, send_count);
   return fk::launch_status("fk_ep_plan");
 }
 

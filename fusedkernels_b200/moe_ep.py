@@ -185,9 +185,11 @@ class _EPMoEFn(torch.autograd.Function):
         src_pos = torch.empty(T, N, **i32)
         send_count = torch.empty(N, **i32)
         perr = torch.zeros(1, **i32)
+        pws = torch.empty(_lib.ep_plan_workspace_bytes(T, N), dtype=torch.uint8, device=dev)
         _lib.call("fk_ep_plan", idx.data_ptr(), w.data_ptr(), T, k, layer.expert_rank.data_ptr(),
                   layer.expert_local.data_ptr(), E, N, send_token.data_ptr(), send_e.data_ptr(),
-                  send_w.data_ptr(), src_pos.data_ptr(), send_count.data_ptr(), perr.data_ptr(), st)
+                  send_w.data_ptr(), src_pos.data_ptr(), send_count.data_ptr(), pws.data_ptr(),
+                  pws.numel(), perr.data_ptr(), st)
         px = layer._peer(T, d, k, dev) if layer.transport == "peer" else None
         if px is not None:
             _lib.call("fk_ep_peer_put_rows", x.data_ptr(), d, send_token.data_ptr(), T, N, ex.rank,

@@ -226,14 +226,19 @@ FK_API int fk_moe_route_meta_skip(const int* idx, const float* w, int64_t n_toke
  * fk_ep_plan: for every destination rank d, the stable list of local tokens with at least
  *   one slot on d (send_token[d*T + i]), each row's k slot entries (send_e = d's local
  *   expert id or -1, send_w = routing weight), src_pos[t*n_ranks + d] (row of token t in
- *   d's list or -1) and send_count[d].  expert_rank/expert_local: [E] placement tables.
+ *   d's list or -1) and send_count[d].  expert_rank/expert_local: [E] placement tables
+ *   (expert_local[e] = e's index among the experts of its owner).  Two passes over chunks
+ *   of 256 tokens (per-chunk counts, then positions); workspace from
+ *   fk_ep_plan_workspace_size.  n_ranks <= 32.
  * fk_ep_pack: send_x[r, :] = x[send_token[r], :] (rows with no token are left untouched).
  * fk_ep_unpack_sum: out[t, :] = sum_d back[d*T + src_pos[t, d], :] in rank order (fp32).
  * fk_ep_unpack_dw: dw[t, j] = back_dw[(d*T + src_pos[t, d])*k + j], d = rank of idx[t, j]. */
+FK_API int fk_ep_plan_workspace_size(int64_t n_tokens, int n_ranks, size_t* bytes);
 FK_API int fk_ep_plan(const int64_t* idx, const float* w, int64_t n_tokens, int k,
                       const int* expert_rank, const int* expert_local, int n_experts,
                       int n_ranks, int* send_token, int* send_e, float* send_w, int* src_pos,
-                      int* send_count, int* err_flag, void* stream);
+                      int* send_count, void* workspace, size_t ws_bytes, int* err_flag,
+                      void* stream);
 FK_API int fk_ep_pack(const void* x, int dim, const int* send_token, int64_t rows, void* send_x,
                       int dtype, void* stream);
 FK_API int fk_ep_unpack_sum(const void* back, int dim, const int* src_pos, int64_t n_tokens,

@@ -29,7 +29,8 @@ def _free_port():
     return p
 
 
-@pytest.mark.parametrize("n_ranks,T,k,E", [(2, 300, 2, 8), (8, 1000, 8, 128), (8, 5, 2, 64)])
+@pytest.mark.parametrize("n_ranks,T,k,E", [(2, 300, 2, 8), (8, 1000, 8, 128), (8, 5, 2, 64),
+                                             (4, 4096, 8, 128), (32, 777, 4, 64)])
 def test_ep_plan_pack_unpack_match_reference(n_ranks, T, k, E):
     G = gen(T + E)
     w, idx = route_oracle(torch.randn(T, E, generator=G), k)
@@ -49,9 +50,10 @@ def test_ep_plan_pack_unpack_match_reference(n_ranks, T, k, E):
     err = torch.zeros(1, **i32)
     st = torch.cuda.current_stream().cuda_stream
     idx_d, w_d, er_d, el_d = idx.to(DEV), w.to(DEV), er.to(DEV), el.to(DEV)
+    ws = torch.empty(_lib.ep_plan_workspace_bytes(T, n_ranks), dtype=torch.uint8, device=DEV)
     _lib.call("fk_ep_plan", idx_d.data_ptr(), w_d.data_ptr(), T, k, er_d.data_ptr(), el_d.data_ptr(),
               E, n_ranks, send_token.data_ptr(), send_e.data_ptr(), send_w.data_ptr(),
-              src_pos.data_ptr(), count.data_ptr(), err.data_ptr(), st)
+              src_pos.data_ptr(), count.data_ptr(), ws.data_ptr(), ws.numel(), err.data_ptr(), st)
     assert err.item() == 0
     for got, want in zip((send_token, send_e, send_w, src_pos, count), ref):
         assert torch.equal(got.cpu(), want.to(got.dtype)), "plan mismatch"
