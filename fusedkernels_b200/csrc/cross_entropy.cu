@@ -163,6 +163,58 @@ __device__ __forceinline__ void online_add_scalar(Online& o, float x) {
   o.s += exp_shift<T>(x, mn);
 }
 
+// 16-bit packets in pairs: packed max of the raw pairs, packed fp32 FMA/ADD (f32x2) for
+// the exponent arguments and the running sums, so a packet of 8 logits costs 3 packed
+// max, 8 conversions, 4 FFMA2, 8 ex2 and 4 FADD2 (plus 4 FADD2 for sum x with label
+// smoothing).  The running sum is kept as two partial lanes (s.x, s.y).
+template <typename T> struct Pair16;
+template <> struct Pair16<__nv_bfloat16> {
+  using type = __nv_bfloat162;
+  static __device__ __forceinline__ type hmax(type a, type b) { return __hmax2(a, b); }
+  static __device__ __forceinline__ float2 to_f2(type v) { return __bfloat1622float2(v); }
+  static __device__ __forceinline__ type from_f2(float2 v) { return __float22bfloat162_rn(v); }
+};
+template <> struct Pair16<__half> {
+  using type = __half2;
+  static __device__ __forceinline__ type hmax(type a, type b) { return __hmax2(a, b); }
+  static __device__ __forceinline__ float2 to_f2(type v) { return __half22float2(v); }
+  static __device__ __forceinline__ type from_f2(float2 v) { return __float22half2_rn(v); }
+};
+
+template <typename T, bool SX>
+__device__ __forceinline__ void online_add_packet2(float& m, float2& s2, float2& sx2,
+                                                   const Vec16<T>& p) {
+  using P = Pair16<T>;
+  using P2 = typename P::type;
+  constexpr int NP = Vec16<T>::N / 2;
+  const P2* pp = reinterpret_cast<const P2*>(p.e);
+  P2 mx = pp[0];
+#pragma unroll
+  for (int i = 1; i < NP; ++i) mx = P::hmax(mx, pp[i]);
+  const float2 mf = P::to_f2(mx);
+  const float pm = fmaxf(mf.x, mf.y);
+  float2 x[NP];
+#pragma unroll
+  for (int i = 0; i < NP; ++i) x[i] = P::to_f2(pp[i]);
+  if constexpr (SX) {
+#pragma unroll
+    for (int i = 0; i < NP; ++i) sx2 = __fadd2_rn(sx2, x[i]);
+  }
+  if (pm > m) {  // new running max
+    const float sc = (m == -INFINITY) ? 0.f : ex2f((m - pm) * kLog2e);
+    s2 = __fmul2_rn(s2, make_float2(sc, sc));
+    m = pm;
+  }
+  if (m == -INFINITY) return;
+  const float2 L = make_float2(kLog2e, kLog2e);
+  const float2 B = make_float2(-m * kLog2e, -m * kLog2e);
+#pragma unroll
+  for (int i = 0; i < NP; ++i) {
+    const float2 t = __ffma2_rn(x[i], L, B);
+    s2 = __fadd2_rn(s2, make_float2(ex2f(t.x), ex2f(t.y)));
+  }
+}
+
 template <typename T>
 __device__ __forceinline__ Online warp_combine(Online o) {
 #pragma unroll
@@ -244,7 +296,7 @@ __device__ __forceinline__ void stream_row(const T* src, int nvec, uint64_t pol,
   cp_async_wait<0>();
 }
 
-template <typename T>
+template <typename T, bool SX>
 __global__ void __launch_bounds__(kRowThreads, 1) ce_row_kernel(
     const T* __restrict__ logits, int64_t lstride, T* grad, int64_t gstride,
     const int64_t* __restrict__ targets, int64_t n_rows, int n_cols, int64_t ignore_index,
@@ -265,7 +317,17 @@ __global__ void __launch_bounds__(kRowThreads, 1) ce_row_kernel(
     const T* src = logits + row * lstride;
     const int64_t t = targets[row];
     Online o{-INFINITY, 0.f, 0.f};
-    stream_row<T>(src, nvec, keep, ring, [&](int, const Vec16<T>& p) { online_add_packet<T>(o, p); });
+    if constexpr (sizeof(T) == 2) {
+      float m = -INFINITY;
+      float2 s2 = make_float2(0.f, 0.f), sx2 = make_float2(0.f, 0.f);
+      stream_row<T>(src, nvec, keep, ring,
+                    [&](int, const Vec16<T>& p) { online_add_packet2<T, SX>(m, s2, sx2, p); });
+      o.m = m;
+      o.s = s2.x + s2.y;
+      o.sx = sx2.x + sx2.y;
+    } else {
+      stream_row<T>(src, nvec, keep, ring, [&](int, const Vec16<T>& p) { online_add_packet<T>(o, p); });
+    }
     for (int i = nvec * VN + tid; i < n_cols; i += kRowThreads) online_add_scalar<T>(o, Elt<T>::to_f(src[i]));
     o = warp_combine<T>(o);
     if (lane == 0) {
@@ -309,20 +371,52 @@ __global__ void __launch_bounds__(kRowThreads, 1) ce_row_kernel(
         else return ex2f(fmaf(x, kLog2e, -cexp)) - sub;
       };
       const int tv = (t < (int64_t)nvec * VN) ? (int)(t / VN) : -1;
-      stream_row<T>(src, nvec, drop, ring, [&](int vv, const Vec16<T>& p) {
-        float g[VN];
+      if constexpr (sizeof(T) == 2) {
+        using P = Pair16<T>;
+        using P2 = typename P::type;
+        constexpr int NP = VN / 2;
+        const float2 L = make_float2(kLog2e, kLog2e);
+        const float2 C = make_float2(-cexp, -cexp);
+        const float2 NS = make_float2(-sub, -sub);
+        stream_row<T>(src, nvec, drop, ring, [&](int vv, const Vec16<T>& p) {
+          const P2* pp = reinterpret_cast<const P2*>(p.e);
+          float2 g[NP];
 #pragma unroll
-        for (int e = 0; e < VN; ++e) g[e] = gval(Elt<T>::to_f(p.e[e]));
-        if (vv == tv) {
-          const int te = (int)(t - (int64_t)vv * VN);
+          for (int i = 0; i < NP; ++i) {
+            const float2 a = __ffma2_rn(P::to_f2(pp[i]), L, C);
+            g[i] = make_float2(ex2f(a.x), ex2f(a.y));
+            if constexpr (SX) g[i] = __fadd2_rn(g[i], NS);
+          }
+          if (vv == tv) {
+            const int te = (int)(t - (int64_t)vv * VN);
 #pragma unroll
-          for (int e = 0; e < VN; ++e) g[e] -= (e == te) ? hsub : 0.f;
-        }
-        Vec16<T> o2;
+            for (int i = 0; i < NP; ++i) {
+              g[i].x -= (2 * i == te) ? hsub : 0.f;
+              g[i].y -= (2 * i + 1 == te) ? hsub : 0.f;
+            }
+          }
+          Vec16<T> o2;
+          P2* op = reinterpret_cast<P2*>(o2.e);
 #pragma unroll
-        for (int e = 0; e < VN; ++e) o2.e[e] = Elt<T>::from_f(g[e]);
-        st_hint(dst + (int64_t)vv * VN, o2.u, drop);
-      });
+          for (int i = 0; i < NP; ++i) op[i] = P::from_f2(g[i]);
+          st_hint(dst + (int64_t)vv * VN, o2.u, drop);
+        });
+      } else {
+        stream_row<T>(src, nvec, drop, ring, [&](int vv, const Vec16<T>& p) {
+          float g[VN];
+#pragma unroll
+          for (int e = 0; e < VN; ++e) g[e] = gval(Elt<T>::to_f(p.e[e]));
+          if (vv == tv) {
+            const int te = (int)(t - (int64_t)vv * VN);
+#pragma unroll
+            for (int e = 0; e < VN; ++e) g[e] -= (e == te) ? hsub : 0.f;
+          }
+          Vec16<T> o2;
+#pragma unroll
+          for (int e = 0; e < VN; ++e) o2.e[e] = Elt<T>::from_f(g[e]);
+          st_hint(dst + (int64_t)vv * VN, o2.u, drop);
+        });
+      }
       for (int i = nvec * VN + tid; i < n_cols; i += kRowThreads) {
         float g = gval(Elt<T>::to_f(src[i]));
         if ((int64_t)i == t) g -= hsub;
@@ -425,10 +519,10 @@ int fwd_t(const void* logits, int64_t ls, void* grad, int64_t gs, const int64_t*
     if (rowvec) {
       int64_t g = n_rows < (int64_t)num_sms() ? n_rows : (int64_t)num_sms();
       const int smem = kDepth * kRowThreads * 16;
-      cudaFuncSetAttribute(ce_row_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-      ce_row_kernel<T><<<(int)g, kRowThreads, smem, st>>>(lp, ls, gp, gs, targets, n_rows,
-                                                          (int)n_cols, ignore, lsm, n_valid,
-                                                          loss_rows, err);
+      auto* kern = lsm > 0.f ? ce_row_kernel<T, true> : ce_row_kernel<T, false>;
+      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+      kern<<<(int)g, kRowThreads, smem, st>>>(lp, ls, gp, gs, targets, n_rows, (int)n_cols,
+                                              ignore, lsm, n_valid, loss_rows, err);
       int s1 = launch_status("fk_ce_fwd(row)");
       if (s1 != FK_OK) return s1;
     } else {

@@ -196,15 +196,19 @@ __global__ void __launch_bounds__(512) rmsnorm_bwd_reg(const T* __restrict__ dy,
 }
 
 // ------------------------------------------------------------------ TMA ring path -----
-// Rows are staged through a ring of STAGES shared-memory buffers filled by cp.async.bulk
-// (one mbarrier per stage), so a CTA keeps up to STAGES rows of HBM reads in flight
+// Rows are staged through a ring of shared-memory buffers filled by cp.async.bulk (one
+// mbarrier per stage), so a CTA keeps up to a ring's worth of rows of HBM reads in flight
 // without spending registers on them.  Each thread copies its packets out of the stage
 // into registers before the block reduction; the reduction's __syncthreads therefore
-// also frees the stage, and thread 0 immediately refills it with the row STAGES ahead.
+// also frees the stage, and thread 0 immediately refills it with the row a ring ahead.
 // A wait that does not complete within the bound poisons the rest of the CTA's rows
 // with NaN instead of spinning.
 constexpr int kRingThreads = 256;
-constexpr int kRingStages = 4;
+// Ring depths measured on B200 at [16384, 4096] and [16384, 8192] bf16: the forward is
+// fastest with 2 rows per CTA (5.6 / 5.9 TB/s; 4 rows: 5.1 / 5.5, 6 rows: 5.1 / 5.4,
+// register-capping for 6-8 CTAs per SM: slower), the backward with 3-4 row pairs.
+constexpr int kRingStages = 3;  // backward: rows of (dy, x) per CTA
+constexpr int kFwdStages = 2;   // forward: rows of x per CTA
 
 template <typename T>
 __device__ __forceinline__ void ring_issue(unsigned char* stage, uint64_t* bar, const T* src0,
@@ -222,7 +226,7 @@ __global__ void __launch_bounds__(kRingThreads) rmsnorm_fwd_ring(
   using V = Vec16<T>;
   constexpr int N = V::N;
   extern __shared__ __align__(128) unsigned char ring[];
-  __shared__ __align__(8) uint64_t full[kRingStages];
+  __shared__ __align__(8) uint64_t full[kFwdStages];
   __shared__ float red[2][32];
   __shared__ int dead;
   const int tid = threadIdx.x;
@@ -237,21 +241,21 @@ __global__ void __launch_bounds__(kRingThreads) rmsnorm_fwd_ring(
     for (int e = 0; e < N; ++e) wr[j][e] = (v < nvec) ? load_w<W>(w, (int64_t)v * N + e) : 0.f;
   }
   if (tid == 0) {
-    for (int q = 0; q < kRingStages; ++q) ptx::mbar_init(&full[q], 1);
+    for (int q = 0; q < kFwdStages; ++q) ptx::mbar_init(&full[q], 1);
     ptx::fence_mbar_init();
     dead = 0;
   }
   __syncthreads();
   if (tid == 0)
-    for (int q = 0; q < kRingStages; ++q) {
+    for (int q = 0; q < kFwdStages; ++q) {
       const int64_t r = blockIdx.x + q * G;
       if (r < rows) ring_issue<T>(ring + (size_t)q * row_bytes, &full[q], x + r * xs, (const T*)nullptr, row_bytes);
     }
   const float inv_cols = 1.0f / (float)cols;
   int i = 0;
   for (int64_t r = blockIdx.x; r < rows; r += G, ++i) {
-    const int q = i % kRingStages;
-    const bool ok = !dead && ptx::mbar_wait(&full[q], (uint32_t)((i / kRingStages) & 1));
+    const int q = i % kFwdStages;
+    const bool ok = !dead && ptx::mbar_wait(&full[q], (uint32_t)((i / kFwdStages) & 1));
     const V* sv = reinterpret_cast<const V*>(ring + (size_t)q * row_bytes);
     V cur[VPT];
     float ss = 0.f;
@@ -269,7 +273,7 @@ __global__ void __launch_bounds__(kRingThreads) rmsnorm_fwd_ring(
     const float tot = block_sum(ss, red[i & 1], kRingThreads / 32);  // also frees stage q
     if (tid == 0) {
       if (!ok) dead = 1;
-      const int64_t rn = r + kRingStages * G;
+      const int64_t rn = r + kFwdStages * G;
       if (!dead && rn < rows)
         ring_issue<T>(ring + (size_t)q * row_bytes, &full[q], x + rn * xs, (const T*)nullptr, row_bytes);
     }
@@ -284,6 +288,91 @@ __global__ void __launch_bounds__(kRingThreads) rmsnorm_fwd_ring(
         for (int e = 0; e < N; ++e) o.e[e] = Elt<T>::from_f(Elt<T>::to_f(cur[j].e[e]) * rs * wr[j][e]);
         st_stream(y + r * ys + (int64_t)v * N, o);
       }
+    }
+  }
+}
+
+// Forward, warp rings: every warp owns kWarpStages shared-memory row buffers filled by
+// cp.async.bulk (one mbarrier each) and walks its own rows, reducing the sum of squares
+// with shuffles, so no row waits on a CTA-wide barrier.  x is read twice from shared
+// memory (sum of squares, then the scaled output), which keeps the registers independent
+// of the row length; the weight row sits in shared memory (fp32) for the whole kernel.
+constexpr int kWarpStages = 3;
+
+template <typename T, typename W>
+__global__ void __launch_bounds__(256) rmsnorm_fwd_warp(
+    const T* __restrict__ x, int64_t xs, const void* __restrict__ w, T* __restrict__ y,
+    int64_t ys, float* __restrict__ rstd, int64_t rows, int cols, float eps) {
+  using V = Vec16<T>;
+  constexpr int N = V::N;
+  extern __shared__ __align__(128) unsigned char smem[];
+  __shared__ __align__(8) uint64_t full[8][kWarpStages];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+  const int nvec = cols / N;
+  const uint32_t row_bytes = (uint32_t)cols * sizeof(T);
+  float* wsm = reinterpret_cast<float*>(smem);  // [cols] fp32, then the warps' stages
+  unsigned char* stages = smem + (((size_t)cols * 4 + 127) / 128) * 128 +
+                          (size_t)warp * kWarpStages * row_bytes;
+  for (int c = threadIdx.x; c < cols; c += blockDim.x) wsm[c] = load_w<W>(w, c);
+  if (lane == 0) {
+    for (int q = 0; q < kWarpStages; ++q) ptx::mbar_init(&full[warp][q], 1);
+    ptx::fence_mbar_init();
+  }
+  __syncthreads();
+  const int64_t G = (int64_t)gridDim.x * nwarps;  // warps in the grid
+  const int64_t first = (int64_t)blockIdx.x * nwarps + warp;
+  if (lane == 0)
+    for (int q = 0; q < kWarpStages; ++q) {
+      const int64_t r = first + q * G;
+      if (r < rows)
+        ring_issue<T>(stages + (size_t)q * row_bytes, &full[warp][q], x + r * xs,
+                      (const T*)nullptr, row_bytes);
+    }
+  const float inv_cols = 1.0f / (float)cols;
+  bool dead = false;
+  int i = 0;
+  for (int64_t r = first; r < rows; r += G, ++i) {
+    const int q = i % kWarpStages;
+    const bool ok = !dead && ptx::mbar_wait(&full[warp][q], (uint32_t)((i / kWarpStages) & 1));
+    const V* sv = reinterpret_cast<const V*>(stages + (size_t)q * row_bytes);
+    float ss = 0.f;
+#pragma unroll 4
+    for (int v = lane; v < nvec; v += 32) {
+      const V p = sv[v];
+#pragma unroll
+      for (int e = 0; e < N; ++e) {
+        const float f = Elt<T>::to_f(p.e[e]);
+        ss = fmaf(f, f, ss);
+      }
+    }
+    ss = warp_sum(ss);
+    const float rs = ok ? rsqrtf(ss * inv_cols + eps) : __int_as_float(0x7fc00000);
+    if (lane == 0) rstd[r] = rs;
+#pragma unroll 4
+    for (int v = lane; v < nvec; v += 32) {
+      const V p = sv[v];
+      const float4* wp = reinterpret_cast<const float4*>(wsm + (size_t)v * N);
+      float wv[N];
+#pragma unroll
+      for (int e4 = 0; e4 < N / 4; ++e4) {
+        const float4 t4 = wp[e4];
+        wv[4 * e4] = t4.x;
+        wv[4 * e4 + 1] = t4.y;
+        wv[4 * e4 + 2] = t4.z;
+        wv[4 * e4 + 3] = t4.w;
+      }
+      V o;
+#pragma unroll
+      for (int e = 0; e < N; ++e) o.e[e] = Elt<T>::from_f(Elt<T>::to_f(p.e[e]) * rs * wv[e]);
+      st_stream(y + r * ys + (int64_t)v * N, o);
+    }
+    __syncwarp();  // every lane is done with stage q
+    if (!ok) dead = true;
+    if (lane == 0) {
+      const int64_t rn = r + kWarpStages * G;
+      if (!dead && rn < rows)
+        ring_issue<T>(stages + (size_t)q * row_bytes, &full[warp][q], x + rn * xs,
+                      (const T*)nullptr, row_bytes);
     }
   }
 }
@@ -525,8 +614,19 @@ int fwd_t(const void* x, int64_t xs, const void* w, void* y, int64_t ys, float* 
   const T* xp = static_cast<const T*>(x);
   T* yp = static_cast<T*>(y);
   const int rv = ring_vpt(cols, sizeof(T), al);
-  if (rv > 0) {
-    const int smem = kRingStages * (int)(cols * sizeof(T));
+  if (rv > 0 && cols * (int64_t)sizeof(T) <= 4096) {
+    // Rows of at most 4 KB: warp rings (measured on B200: 1.4x the CTA ring at 2 KB rows,
+    // 1.04x at 4 KB; the CTA ring wins from 8 KB rows on, where a warp's row takes too
+    // long at 8 warps per SM).  8 warps x kWarpStages rows + the fp32 weight row.
+    const int wbytes = (int)(((cols * 4 + 127) / 128) * 128);
+    const int nw = 8;
+    const int smem = wbytes + nw * kWarpStages * (int)(cols * sizeof(T));
+    auto k = rmsnorm_fwd_warp<T, W>;
+    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    k<<<persistent_grid(k, nw * 32, rows, smem), nw * 32, smem, s>>>(xp, xs, w, yp, ys, rstd,
+                                                                     rows, (int)cols, eps);
+  } else if (rv > 0) {
+    const int smem = kFwdStages * (int)(cols * sizeof(T));
     switch (rv) {
 #define FK_CASE(V)                                                                      \
   case V: {                                                                             \

@@ -8,11 +8,14 @@ the eager PyTorch formulation of the same ops.  Attention and the linear layers 
 PyTorch's (SDPA / cuBLAS) in both modes.
 
 ``train_step`` runs forward, backward and an AdamW step; ``python -m
-fusedkernels_b200.mini_gpt --mode fused`` prints tokens/s.
+fusedkernels_b200.mini_gpt --mode fused`` prints tokens/s.  Under torchrun every rank trains
+its own batch and DistributedDataParallel all-reduces the gradients of the replicated
+parameters (data parallelism); tokens/s is then the sum over ranks.
 """
 from __future__ import annotations
 
 import argparse
+import os
 import time
 
 import torch
@@ -115,11 +118,19 @@ def main():
     ap.add_argument("--batch-size", type=int, default=8)
     ap.add_argument("--seq-len", type=int, default=1024)
     args = ap.parse_args()
-    dev = torch.device("cuda")
-    torch.manual_seed(0)
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    torch.cuda.set_device(dev)
+    if world > 1:
+        torch.distributed.init_process_group("nccl", device_id=dev)
+    torch.manual_seed(0)  # identical initial weights on every rank
     model = MiniGPT(max_seq_len=args.seq_len, fused=args.mode == "fused").to(dev, torch.bfloat16)
-    opt = torch.optim.AdamW(model.parameters(), lr=3e-4)
     V = model.lm_head.out_features
+    if world > 1:
+        model = torch.nn.parallel.DistributedDataParallel(model, device_ids=[dev.index])
+    opt = torch.optim.AdamW(model.parameters(), lr=3e-4)
+    torch.manual_seed(1000 + rank)  # each rank draws its own batches
     for _ in range(args.warmup):
         idx = torch.randint(0, V, (args.batch_size, args.seq_len + 1), device=dev)
         train_step(model, opt, idx[:, :-1], idx[:, 1:])
@@ -130,8 +141,15 @@ def main():
         loss = train_step(model, opt, idx[:, :-1], idx[:, 1:])
     torch.cuda.synchronize()
     dt = time.perf_counter() - t0
-    print(f"mode={args.mode} tokens/s={args.steps * args.batch_size * args.seq_len / dt:,.0f} "
-          f"loss={loss.item():.4f}")
+    if world > 1:
+        t = torch.tensor([dt], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        dt = float(t.item())
+    if rank == 0:
+        tok = world * args.steps * args.batch_size * args.seq_len
+        print(f"mode={args.mode} ranks={world} tokens/s={tok / dt:,.0f} loss={loss.item():.4f}")
+    if world > 1:
+        torch.distributed.destroy_process_group()
 
 
 if __name__ == "__main__":
