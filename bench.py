@@ -559,18 +559,22 @@ class MoELayer(Workload):
                 layer.w13[:, H:].copy_(wu)
                 layer.w2.copy_(wd)
             self.placement = None
+            self.replicated = []
             T0, T1 = 0, self.tokens
         else:
-            from fusedkernels_b200.moe_ep import ExpertParallelMoEMLP, lpt_placement
+            from fusedkernels_b200.moe_ep import (ExpertParallelMoEMLP, hot_experts,
+                                                  lpt_placement_excluding)
             # Load-aware static placement from the expert loads of this batch (computed
             # identically on every rank from the same full batch: no communication).
             with torch.no_grad():
                 logits = x_all.to(dev) @ wr.t() + bias
                 _, idx = fk.fused_moe_route_v2(logits, self.k)
                 load = torch.bincount(idx.reshape(-1), minlength=E).float().cpu()
-            self.placement = lpt_placement(load.tolist(), self.world)
+            self.replicated = hot_experts(load.tolist(), self.world)
+            self.placement = lpt_placement_excluding(load.tolist(), self.world, self.replicated)
             layer = ExpertParallelMoEMLP(D, H, E, self.k, placement=self.placement,
-                                         transport=self.ep_transport).to(dev).bfloat16()
+                                         transport=self.ep_transport,
+                                         replicated=self.replicated).to(dev).bfloat16()
             layer.load_from_full(wr, wg, wu, wd)
             per = self.tokens // self.world
             T0, T1 = self.rank * per, (self.rank + 1) * per
@@ -667,8 +671,9 @@ class MoELayer(Workload):
 
     def config(self):
         par = "single GPU" if self.world == 1 else (
-            f"ep{self.world}: {self.E // self.world} experts per GPU, load-aware (LPT) static "
-            f"placement, dispatch/combine "
+            f"ep{self.world}: {len(self.replicated)} hot experts replicated on every GPU "
+            f"(gradients all-reduced), the other {self.E - len(self.replicated)} placed by "
+            f"load-aware LPT bin packing, dispatch/combine "
             + ("by put kernels into peer memory over NVLink" if self.ep_transport == "peer"
                else "by NCCL all-to-all") + f"; {self.tokens // self.world} tokens per GPU")
         return {"workload": "moe_sorted_dispatch_fwd_bwd", "tokens": self.tokens, "dim": self.dim,

@@ -36,6 +36,7 @@ namespace fk {
 namespace {
 
 constexpr int kPutThreads = 256;
+constexpr int kPutBatch = 8;  // 16-byte packets per lane in flight in the row copy
 
 // ctl layout (uint32, local to each rank): [phase]       ticket of the put kernels
 //                                          [8 + phase]   sequence numbers published
@@ -103,7 +104,21 @@ __global__ void __launch_bounds__(kPutThreads) ep_peer_put_rows_kernel(
     if (t >= 0) {
       const T_* src = x + (int64_t)t * dim;
       T_* dst = static_cast<T_*>(row_bases[d]) + dst_row * dim;
-      for (int v = lane; v < nvec; v += 32) st_plain(dst + v * V::N, ld_keep(src + v * V::N));
+      // kPutBatch packets per lane are loaded before any is stored, so every lane keeps
+      // that many loads in flight ahead of its NVLink stores.
+      for (int v0 = 0; v0 < nvec; v0 += 32 * kPutBatch) {
+        V buf[kPutBatch];
+#pragma unroll
+        for (int b = 0; b < kPutBatch; ++b) {
+          const int v = v0 + b * 32 + lane;
+          if (v < nvec) buf[b] = ld_keep(src + v * V::N);
+        }
+#pragma unroll
+        for (int b = 0; b < kPutBatch; ++b) {
+          const int v = v0 + b * 32 + lane;
+          if (v < nvec) st_plain(dst + v * V::N, buf[b]);
+        }
+      }
     }
     if (send_e != nullptr) {
       for (int j = lane; j < k; j += 32) {

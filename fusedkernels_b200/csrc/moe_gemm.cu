@@ -41,6 +41,7 @@ namespace gemm {
 constexpr int BM = 128;
 constexpr int BK = 64;
 constexpr int kThreads = 192;
+constexpr int kMaxGemmExperts = 256;  // expert ids of the weight-gradient schedule fit a byte
 constexpr uint64_t kWaitNs = 2000000000ull;  // 2 s per wait: far above any legitimate wait
 
 enum Mode { MODE_M = 0, MODE_K = 1 };
@@ -236,8 +237,13 @@ __device__ __forceinline__ int num_tiles(const Params& p) {
   return p.E * nmb * nnb;
 }
 
+// MODE_K visits the experts in descending order of their token count (order[]) and hands
+// the tiles out in a serpentine over the CTAs (pass i goes left to right when i is even,
+// right to left when odd), so the tiles of the few hot experts of a skewed routing spread
+// evenly over the SMs instead of piling up on the CTAs their position happens to hit.
+// t runs over whole passes; tiles past the end are invalid.
 template <int BN, int MODE, int EPI>
-__device__ __forceinline__ Tile decode(const Params& p, int t) {
+__device__ __forceinline__ Tile decode(const Params& p, int t, const uint8_t* order, int ntiles) {
   Tile tl;
   tl.valid = true;
   if (MODE == MODE_M) {
@@ -251,8 +257,14 @@ __device__ __forceinline__ Tile decode(const Params& p, int t) {
     tl.kiters = p.K / BK;
   } else {
     const int nmb = (p.M + BM - 1) / BM, nnb = p.N / BN;
-    tl.e = t / (nmb * nnb);
-    const int r = t % (nmb * nnb);
+    const int G = gridDim.x, pass = t / G, j = t % G;
+    const int g = pass * G + ((pass & 1) ? G - 1 - j : j);
+    if (g >= ntiles) {
+      tl.valid = false;
+      return tl;
+    }
+    tl.e = order[g / (nmb * nnb)];
+    const int r = g % (nmb * nnb);
     tl.m0 = (r / nnb) * BM;
     tl.n0 = (r % nnb) * BN;
     const int s0 = p.seg_start[tl.e], s1 = p.seg_start[tl.e + 1];
@@ -283,6 +295,18 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  __shared__ uint8_t order[kMaxGemmExperts];  // MODE_K: experts by descending token count
+  if (MODE == MODE_K) {
+    for (int e = threadIdx.x; e < p.E; e += blockDim.x) {
+      const int len = p.seg_start[e + 1] - p.seg_start[e];
+      int rank = 0;
+      for (int f = 0; f < p.E; ++f) {
+        const int lf = p.seg_start[f + 1] - p.seg_start[f];
+        rank += (lf > len) || (lf == len && f < e);
+      }
+      order[rank] = (uint8_t)e;
+    }
+  }
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       ptx::mbar_init(&full[s], 1);
@@ -306,6 +330,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   const int ntiles = num_tiles<BN, MODE, EPI>(p);
+  const int tiles_loop =
+      MODE == MODE_K ? (ntiles + (int)gridDim.x - 1) / (int)gridDim.x * (int)gridDim.x : ntiles;
 
   if (warp == 0) {
     if (lane == 0) {
@@ -313,8 +339,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       int s = 0;
       uint32_t ph = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
-        const Tile tl = decode<BN, MODE, EPI>(p, t);
+      for (int t = blockIdx.x; t < tiles_loop && ok; t += gridDim.x) {
+        const Tile tl = decode<BN, MODE, EPI>(p, t, order, ntiles);
         if (!tl.valid) continue;
         for (int kb = 0; kb < tl.kiters; ++kb) {
           if (!wait_bar(&empty[s], ph ^ 1, p.err, 11)) { ok = false; break; }
@@ -354,8 +380,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t ph = 0;
       int it = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
-        const Tile tl = decode<BN, MODE, EPI>(p, t);
+      for (int t = blockIdx.x; t < tiles_loop && ok; t += gridDim.x) {
+        const Tile tl = decode<BN, MODE, EPI>(p, t, order, ntiles);
         if (!tl.valid) continue;
         const int acc = it & 1;
         const uint32_t aph = (uint32_t)((it >> 1) & 1);
@@ -392,8 +418,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int row_in_tile = q * 32 + lane;
     StoreRing ring{ring_base + (uint32_t)(warp - 2) * kRingBytesPerWarp, 0};
     int it = 0;
-    for (int t = blockIdx.x; t < ntiles; t += gridDim.x) {
-      const Tile tl = decode<BN, MODE, EPI>(p, t);
+    for (int t = blockIdx.x; t < tiles_loop; t += gridDim.x) {
+      const Tile tl = decode<BN, MODE, EPI>(p, t, order, ntiles);
       if (!tl.valid) continue;
       const int acc = it & 1;
       const uint32_t aph = (uint32_t)((it >> 1) & 1);
@@ -748,7 +774,8 @@ extern "C" int fk_moe_gemm_wgrad(const void* a, int m_dim, const void* b, int n_
                                  int* err_flag, void* stream) {
   FK_CHECK_ARG(a && b && seg_start && dw && err_flag, "fk_moe_gemm_wgrad: null pointer");
   FK_CHECK_ARG(max_rows >= 0 && max_rows % G::BM == 0, "fk_moe_gemm_wgrad: max_rows must be a multiple of 128");
-  FK_CHECK_ARG(n_experts >= 1 && m_dim % 64 == 0 && n_dim % 64 == 0 && m_dim > 0 && n_dim > 0,
+  FK_CHECK_ARG(n_experts >= 1 && n_experts <= G::kMaxGemmExperts && m_dim % 64 == 0 &&
+                   n_dim % 64 == 0 && m_dim > 0 && n_dim > 0,
                "fk_moe_gemm_wgrad: dims must be positive multiples of 64");
   FK_CHECK_ARG(fk::aligned16(a) && fk::aligned16(b) && fk::aligned16(dw), "fk_moe_gemm_wgrad: unaligned");
   const int bn = G::pick_bn(n_dim);

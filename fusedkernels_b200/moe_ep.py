@@ -58,6 +58,56 @@ def round_robin_placement(n_experts: int, n_ranks: int) -> list[int]:
     return [e % n_ranks for e in range(n_experts)]
 
 
+def hot_experts(load, n_ranks: int, fraction: float = 0.25) -> list[int]:
+    """Experts worth replicating on every rank: those whose load alone exceeds `fraction`
+    of one rank's fair share of all assignments.  Such an expert is picked by a large
+    share of all tokens, so owning it on one rank makes that rank receive nearly every
+    token of every other rank; replicated, its slots are computed where the token lives
+    and only its weight gradient (25 MB at D=4096, H=1024) is summed across ranks."""
+    load = [float(v) for v in load]
+    if n_ranks <= 1:
+        return []
+    share = sum(load) / n_ranks
+    return sorted(e for e, v in enumerate(load) if v >= fraction * share)
+
+
+def plan_tables(placement, replicated, n_ranks: int, rank: int):
+    """Stack and planning tables of one rank.
+
+    Returns (local_ids, n_owned, expert_rank, expert_local): the rank's stacked experts
+    (owned ones by ascending id, then the replicated ones), how many it owns, and for every
+    expert e the rank that computes e's slots for a token of this rank (the owner, or this
+    rank for a replicated expert) with e's index inside that rank's stack."""
+    E = len(placement)
+    rep_set = set(replicated)
+    rep_sorted = sorted(rep_set)
+    owned = [e for e in range(E) if e not in rep_set and placement[e] == rank]
+    cold_place = [placement[e] if e not in rep_set else n_ranks for e in range(E)]
+    cold_index = owner_local_index(cold_place, n_ranks + 1)
+    expert_rank = [rank if e in rep_set else placement[e] for e in range(E)]
+    expert_local = [len(owned) + rep_sorted.index(e) if e in rep_set else cold_index[e]
+                    for e in range(E)]
+    return owned + rep_sorted, len(owned), expert_rank, expert_local
+
+
+def lpt_placement_excluding(load, n_ranks: int, replicated) -> list[int]:
+    """LPT placement of the experts that are not replicated, at most
+    ceil(n_cold / n_ranks) per rank; replicated experts get -1."""
+    load = [float(v) for v in load]
+    rep = set(replicated)
+    cold = [e for e in range(len(load)) if e not in rep]
+    cap = -(-len(cold) // n_ranks)
+    tot = [0.0] * n_ranks
+    used = [0] * n_ranks
+    rank_of = [-1] * len(load)
+    for e in sorted(cold, key=lambda i: (-load[i], i)):
+        r = min((r for r in range(n_ranks) if used[r] < cap), key=lambda r: (tot[r], r))
+        rank_of[e] = r
+        tot[r] += load[e]
+        used[r] += 1
+    return rank_of
+
+
 def owner_local_index(placement, n_ranks: int) -> list[int]:
     """For every expert, its position among the experts of the rank that owns it (the
     order of that rank's stacked weights: ascending global id)."""
@@ -300,10 +350,25 @@ class _EPMoEFn(torch.autograd.Function):
                       k, dx_part.data_ptr(), _lib.FK_BF16, st)
             back_dx, w1 = ex.all_to_all(dx_part, async_op=True)
             back_dw, w2 = ex.all_to_all(dw_recv, async_op=True)
-        _lib.call("fk_moe_gemm_wgrad", dy.data_ptr(), d, act.data_ptr(), H, R,
-                  plan.seg_start.data_ptr(), El, dw2.data_ptr(), eptr + 4, st)
-        _lib.call("fk_moe_gemm_wgrad", dh1.data_ptr(), 2 * H, xs.data_ptr(), d, R,
-                  plan.seg_start.data_ptr(), El, dw13.data_ptr(), eptr + 4, st)
+        # Replicated experts sit at the end of the stack: their gradients are computed first
+        # and summed over the group while the owned experts' gradients are computed.
+        n_own = layer.n_owned
+        seg = plan.seg_start
+        parts = [(n_own, El), (0, n_own)] if layer.replicated and N > 1 else [(0, El)]
+        red = None
+        for lo, hi in parts:
+            if hi <= lo:
+                continue
+            _lib.call("fk_moe_gemm_wgrad", dy.data_ptr(), d, act.data_ptr(), H, R,
+                      seg.data_ptr() + 4 * lo, hi - lo, dw2[lo].data_ptr(), eptr + 4, st)
+            _lib.call("fk_moe_gemm_wgrad", dh1.data_ptr(), 2 * H, xs.data_ptr(), d, R,
+                      seg.data_ptr() + 4 * lo, hi - lo, dw13[lo].data_ptr(), eptr + 4, st)
+            if lo == n_own and hi > lo:
+                red = [dist.all_reduce(dw13[lo:hi], group=ex.group, async_op=True),
+                       dist.all_reduce(dw2[lo:hi], group=ex.group, async_op=True)]
+        if red is not None:
+            for wk in red:
+                wk.wait()
         if px is not None:
             px.wait(px.PHASE_BWD_COMBINE, st)
             back_dx_p, back_dw_p = px.local("to_source"), px.local("dw")
@@ -326,11 +391,15 @@ class _EPMoEFn(torch.autograd.Function):
 class ExpertParallelMoEMLP(nn.Module):
     """``FusedMoEMLPSorted`` with its experts sharded over a process group (see module doc).
 
-    placement: expert -> rank list (default ``round_robin_placement``).  Every rank must
-    construct the layer with the same placement."""
+    placement: expert -> rank list (default ``round_robin_placement``).  replicated:
+    experts held by every rank (their slots are computed on the token's own rank; their
+    weight gradients are summed over the group inside backward, so every copy receives
+    the full-batch gradient); their placement entries are ignored.  Every rank must
+    construct the layer with the same placement and replicated set."""
 
     def __init__(self, dim: int, hidden_dim: int, n_experts: int, k: int = 2, group=None,
-                 placement=None, router_version: str = "v2", transport: str = "peer"):
+                 placement=None, router_version: str = "v2", transport: str = "peer",
+                 replicated=()):
         super().__init__()
         assert router_version == "v2"
         assert transport in ("peer", "nccl")
@@ -340,16 +409,20 @@ class ExpertParallelMoEMLP(nn.Module):
         self.exchange = Exchange(group)
         N, r = self.exchange.world, self.exchange.rank
         placement = list(placement) if placement is not None else round_robin_placement(n_experts, N)
-        assert len(placement) == n_experts and all(0 <= p < N for p in placement)
+        self.replicated = sorted(set(int(e) for e in replicated))
+        rep_set = set(self.replicated)
+        assert len(placement) == n_experts
+        assert all(0 <= placement[e] < N for e in range(n_experts) if e not in rep_set)
+        assert all(0 <= e < n_experts for e in self.replicated)
         self.placement = placement
-        self.local_ids = [e for e in range(n_experts) if placement[e] == r]
+        self.local_ids, self.n_owned, rank_tab, local_tab = plan_tables(
+            placement, self.replicated, N, r)
         self.router = nn.Linear(dim, n_experts, bias=False)
         self.experts = nn.ModuleDict({str(e): Expert(dim, hidden_dim) for e in self.local_ids})
-        self.register_buffer("expert_rank", torch.tensor(placement, dtype=torch.int32), persistent=False)
-        # index of every expert inside its OWNER's stacked weights (the destination rank of
-        # a slot looks its expert up in this table when the slot is planned)
-        self.register_buffer("expert_local", torch.tensor(owner_local_index(placement, N),
-                                                          dtype=torch.int32), persistent=False)
+        self.register_buffer("expert_rank", torch.tensor(rank_tab, dtype=torch.int32),
+                             persistent=False)
+        self.register_buffer("expert_local", torch.tensor(local_tab, dtype=torch.int32),
+                             persistent=False)
         self._restack()
 
     def _expert_params(self):

@@ -187,7 +187,7 @@ def test_ep_peer_wait_times_out_and_reports():
     assert (torch.ones(4, device=DEV) * 2).sum().item() == 8.0
 
 
-def _ep_worker(rank, world, port, q, transport="peer"):
+def _ep_worker(rank, world, port, q, transport="peer", replicated=()):
     import sys
     root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
     sys.path.insert(0, root)
@@ -205,7 +205,7 @@ def _ep_worker(rank, world, port, q, transport="peer"):
         x_all = torch.randn(world * T, D, generator=G).bfloat16()
         d_all = torch.randn(world * T, D, generator=G).bfloat16()
         ep = ExpertParallelMoEMLP(D, H, E, k, placement=lpt_placement([1.0] * E, world),
-                                  transport=transport).to(dev).bfloat16()
+                                  transport=transport, replicated=replicated).to(dev).bfloat16()
         ep.load_from_full(*(t.bfloat16().to(dev) for t in wts))
         x = x_all[rank * T:(rank + 1) * T].to(dev).requires_grad_(True)
         out = ep(x)
@@ -214,24 +214,26 @@ def _ep_worker(rank, world, port, q, transport="peer"):
             _, idx = fused_moe_route_v2(ep.router(x.detach()), k)
         torch.cuda.synchronize()
         assert ep.peer_error() == 0, f"peer wait timed out: {ep.peer_error()}"
+        grads = {e: tuple(getattr(ep.experts[str(e)], n).weight.grad.float().cpu()
+                          for n in ("w_gate", "w_up", "w_down")) for e in ep.local_ids}
         ep.close()
-        q.put((rank, out.detach().float().cpu(), x.grad.detach().float().cpu(), idx.cpu()))
+        q.put((rank, out.detach().float().cpu(), x.grad.detach().float().cpu(), idx.cpu(), grads))
     except Exception as exc:
-        q.put((rank, repr(exc), None, None))
+        q.put((rank, repr(exc), None, None, None))
     finally:
         if dist.is_initialized():
             dist.destroy_process_group()
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("transport", ["peer", "nccl"])
-def test_ep_layer_two_ranks_matches_single_gpu(transport):
+@pytest.mark.parametrize("transport,replicated", [("peer", ()), ("nccl", ()), ("peer", (0, 5))])
+def test_ep_layer_two_ranks_matches_single_gpu(transport, replicated):
     import torch.multiprocessing as mp
     D, H, E, k, T, world = 256, 256, 16, 4, 256, 2
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_ep_worker, args=(r, world, port, q, transport))
+    procs = [ctx.Process(target=_ep_worker, args=(r, world, port, q, transport, replicated))
              for r in range(world)]
     for p in procs:
         p.start()
@@ -247,6 +249,7 @@ def test_ep_layer_two_ranks_matches_single_gpu(transport):
     # Tokens are independent, so the single-GPU layer runs on each rank's T tokens: the
     # router GEMM then has the same shape on both sides and the bf16 logits (and with them
     # the expert selection, which a 1-ulp difference on a near-tie would flip) are equal.
+    ref_grads = {}
     for r in res:
         sl = slice(r[0] * T, (r[0] + 1) * T)
         layer, ref_out, ref_dx = _single_gpu(D, H, E, k, wts, x_all[sl], d_all[sl])
@@ -257,3 +260,15 @@ def test_ep_layer_two_ranks_matches_single_gpu(transport):
         assert (r[1] - ref_out.float().cpu()).abs().max().item() <= 2e-2 * scale, f"rank {r[0]} out"
         scale = ref_dx.abs().max().item()
         assert (r[2] - ref_dx.float().cpu()).abs().max().item() <= 2e-2 * scale, f"rank {r[0]} dx"
+        for e in range(E):  # expert gradients: the sum of the chunks' gradients
+            ex = layer.experts[e]
+            g = tuple(getattr(ex, n).weight.grad.float().cpu() for n in ("w_gate", "w_up", "w_down"))
+            ref_grads[e] = g if e not in ref_grads else tuple(a + b for a, b in zip(ref_grads[e], g))
+    held = set()
+    for r in res:
+        for e, g in r[4].items():
+            held.add(e)
+            for a, b in zip(g, ref_grads[e]):
+                scale = max(b.abs().max().item(), 1e-6)
+                assert (a - b).abs().max().item() <= 3e-2 * scale, f"rank {r[0]} expert {e} grad"
+    assert held == set(range(E))

@@ -44,6 +44,32 @@ def test_owner_local_index_matches_per_rank_order():
             assert [table[e] for e in ids] == list(range(len(ids)))
 
 
+def test_replication_tables_are_consistent_across_ranks():
+    """Every slot a rank plans for its own tokens lands on a rank whose stack holds that
+    expert at the planned index; replicated experts stay on the token's rank."""
+    from fusedkernels_b200.moe_ep import hot_experts, lpt_placement_excluding, plan_tables
+    from oracle import zipf_expert_bias
+    E = 128
+    load = torch.exp(zipf_expert_bias(E) / 2).tolist()
+    for N in (2, 4, 8):
+        rep = hot_experts(load, N)
+        pl = lpt_placement_excluding(load, N, rep)
+        assert all((pl[e] == -1) == (e in rep) for e in range(E))
+        stacks = {r: plan_tables(pl, rep, N, r)[0] for r in range(N)}
+        assert sorted(e for r in range(N) for e in stacks[r] if e not in rep) == \
+            [e for e in range(E) if e not in rep]
+        for r in range(N):
+            _, n_own, rank_tab, local_tab = plan_tables(pl, rep, N, r)
+            for e in range(E):
+                d = rank_tab[e]
+                assert stacks[d][local_tab[e]] == e
+                if e in rep:
+                    assert d == r
+        counts = [len(stacks[r]) - len(rep) for r in range(N)]
+        assert max(counts) <= -(-(E - len(rep)) // N)
+    assert hot_experts(load, 1) == []
+
+
 def test_lpt_placement_rejects_uneven():
     with pytest.raises(ValueError):
         lpt_placement([1.0] * 10, 4)
