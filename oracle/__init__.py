@@ -2,7 +2,7 @@
 
 This package restates, on the CPU, the PyTorch reference path that the fusedkernels
 repository checks its fused ops against.  It is imported only by tests/, by
-``__graft_entry__.smoke()`` (as the checker) and by bench.py's CPU-baseline and
+``__graft_entry__.smoke()`` (to verify the kernels' results) and by bench.py's CPU-baseline and
 ``--impl reference`` legs.  The product (fusedkernels_b200) never imports it and has no
 CPU fallback.
 
