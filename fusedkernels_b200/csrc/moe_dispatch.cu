@@ -23,6 +23,8 @@
 namespace fk {
 namespace {
 
+constexpr int kRowBatch = 4;  // 16-byte packets per lane loaded ahead in row copies
+
 constexpr int kMetaThreads = 256;
 constexpr int kMetaWarps = kMetaThreads / 32;
 constexpr int kBlockRows = 128;
@@ -172,8 +174,21 @@ __global__ void __launch_bounds__(256) moe_gather_kernel(const T* __restrict__ x
       z.u = make_uint4(0, 0, 0, 0);
       for (int v = lane; v < nvec; v += 32) st_plain(dst + v * V::N, z);
     } else {
+      // kRowBatch packets per lane are loaded before they are stored (loads in flight)
       const T* src = x + (int64_t)(a / k) * dim;
-      for (int v = lane; v < nvec; v += 32) st_plain(dst + v * V::N, ld_keep(src + v * V::N));
+      for (int v0 = 0; v0 < nvec; v0 += 32 * kRowBatch) {
+        V buf[kRowBatch];
+#pragma unroll
+        for (int b = 0; b < kRowBatch; ++b) {
+          const int v = v0 + b * 32 + lane;
+          if (v < nvec) buf[b] = ld_keep(src + v * V::N);
+        }
+#pragma unroll
+        for (int b = 0; b < kRowBatch; ++b) {
+          const int v = v0 + b * 32 + lane;
+          if (v < nvec) st_plain(dst + v * V::N, buf[b]);
+        }
+      }
     }
   }
 }
@@ -239,15 +254,31 @@ __global__ void __launch_bounds__(256) moe_combine_bwd_kernel(
     const T* g = dout + (int64_t)(a / k) * dim;
     const T* yr = y + p * dim;
     float dot = 0.f;
-    for (int v = lane; v < nvec; v += 32) {
-      V gv = ld_keep(g + v * V::N), yv = ld_keep(yr + v * V::N), o;
+    // packets in the same order as one-at-a-time processing (the dot product's summation
+    // order is unchanged), kRowBatch of each operand loaded ahead
+    for (int v0 = 0; v0 < nvec; v0 += 32 * kRowBatch) {
+      V gv[kRowBatch], yv[kRowBatch];
 #pragma unroll
-      for (int i = 0; i < V::N; ++i) {
-        float gf = Elt<T>::to_f(gv.e[i]);
-        dot = fmaf(gf, Elt<T>::to_f(yv.e[i]), dot);
-        o.e[i] = Elt<T>::from_f(wa * gf);
+      for (int b = 0; b < kRowBatch; ++b) {
+        const int v = v0 + b * 32 + lane;
+        if (v < nvec) {
+          gv[b] = ld_keep(g + v * V::N);
+          yv[b] = ld_keep(yr + v * V::N);
+        }
       }
-      st_plain(dst + v * V::N, o);
+#pragma unroll
+      for (int b = 0; b < kRowBatch; ++b) {
+        const int v = v0 + b * 32 + lane;
+        if (v >= nvec) continue;
+        V o;
+#pragma unroll
+        for (int i = 0; i < V::N; ++i) {
+          const float gf = Elt<T>::to_f(gv[b].e[i]);
+          dot = fmaf(gf, Elt<T>::to_f(yv[b].e[i]), dot);
+          o.e[i] = Elt<T>::from_f(wa * gf);
+        }
+        st_plain(dst + v * V::N, o);
+      }
     }
     dot = warp_sum(dot);
     if (lane == 0) dw[a] = dot;
