@@ -117,6 +117,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--batch-size", type=int, default=8)
     ap.add_argument("--seq-len", type=int, default=1024)
+    ap.add_argument("--dim", type=int, default=1024)
+    ap.add_argument("--layers", type=int, default=12)
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -125,7 +127,8 @@ def main():
     if world > 1:
         torch.distributed.init_process_group("nccl", device_id=dev)
     torch.manual_seed(0)  # identical initial weights on every rank
-    model = MiniGPT(max_seq_len=args.seq_len, fused=args.mode == "fused").to(dev, torch.bfloat16)
+    model = MiniGPT(dim=args.dim, n_layers=args.layers, hidden_dim=args.dim * 43 // 16,
+                    max_seq_len=args.seq_len, fused=args.mode == "fused").to(dev, torch.bfloat16)
     V = model.lm_head.out_features
     if world > 1:
         model = torch.nn.parallel.DistributedDataParallel(model, device_ids=[dev.index])

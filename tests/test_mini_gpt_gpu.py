@@ -28,3 +28,23 @@ def test_fused_and_native_mini_gpt_agree_and_train():
         losses[name] = ls
         assert ls[-1] < ls[0]
     assert abs(losses["fused"][-1] - losses["native"][-1]) <= 0.1 * losses["native"][-1]
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_mini_gpt_data_parallel_two_ranks():
+    """The training harness under torchrun: two ranks, DistributedDataParallel over NCCL,
+    fused ops on each rank; the run finishes and rank 0 reports tokens/s and a finite loss."""
+    import os
+    import re
+    import subprocess
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node", "2",
+           "--master-addr", "127.0.0.1", "--master-port", "29617", "-m",
+           "fusedkernels_b200.mini_gpt", "--mode", "fused", "--steps", "3", "--warmup", "1",
+           "--batch-size", "2", "--seq-len", "128", "--dim", "256", "--layers", "2"]
+    r = subprocess.run(cmd, cwd=root, capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stderr[-2000:]
+    m = re.search(r"ranks=2 tokens/s=([\d,]+) loss=([\d.]+)", r.stdout)
+    assert m, r.stdout[-1000:]
+    assert float(m.group(2)) > 0
