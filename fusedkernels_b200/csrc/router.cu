@@ -9,10 +9,10 @@
 // which is below every real key (-inf maps to 0x007FFFFF in the high word).
 //
 // Two kernel families.  For k <= 8 (every routing configuration of the reference's
-// tests and benchmarks; k <= 4 when E > 128) the forward holds a row in a small group of
-// lanes that each select over 8 logits by sorted insertion and merge their lists by a
-// butterfly (the lane-group kernels further down), and for k <= 4 the backward uses the
-// same lane groups.  Otherwise the segment kernels below run a bitonic network.
+// tests and benchmarks) the forward holds a row in a small group of lanes that each
+// select over up to 32 logits by sorted insertion and merge their lists by a butterfly
+// (the lane-group kernels further down), and for k <= 4 the backward uses lane groups of
+// 8 entries per lane.  Otherwise the segment kernels below run a bitonic network.
 //
 // Layout.  A row of E experts is padded to L = S*V (power of two) and held by a
 // segment of S lanes (S = min(32, L)), V keys per lane; element i = r*S + lane.
@@ -249,10 +249,10 @@ __global__ void __launch_bounds__(256) router_fwd_kernel(const T* __restrict__ l
 }
 
 // ---------------------------------------------------------------------------------------
-// Lane-group kernels, k <= 8.  A row is held by a group of G lanes (G = next_pow2(E/8),
-// 1..32), 8 logits per lane: lane l of the group owns the 16-byte packets p*G + l of the
-// row (2 packets of fp32 or 1 of bf16/fp16), so one warp load covers 32/G whole rows.
-// Each lane keeps the top KP = next_pow2(k) (key, expert) pairs of its 8 logits in
+// Lane-group kernels, k <= 8.  A row is held by a group of G lanes (G = next_pow2(E/C),
+// 1..32), C logits per lane (C = 32; 8 / 16 for E <= 8 / 16 and 8 for few rows): lane l owns
+// the 16-byte packets p*G + l of the row, so one warp load covers 32/G whole rows.
+// Each lane keeps the top KP = next_pow2(k) (key, expert) pairs of its C logits in
 // registers by sorted insertion -- its logits arrive in increasing expert order, so a
 // strict '>' keeps the lower index first on ties -- and the G lists are merged by a
 // butterfly over the group: at distance d the partner's list is reversed, the pairwise
@@ -265,7 +265,18 @@ __global__ void __launch_bounds__(256) router_fwd_kernel(const T* __restrict__ l
 // Keys are signed integers: bits ^ ((bits >> 31) & 0x7fffffff) orders like the float and
 // is its own inverse; -0.0 is folded onto +0.0 (x + 0.0f) and every NaN becomes INT_MAX,
 // above +inf (0x7f800000).  Padding is INT_MIN, below -inf (0x807fffff).
-constexpr int kLaneElems = 8;   // logits per lane
+constexpr int kLaneElems = 8;   // dense gradient entries per lane (backward)
+// Logits per lane in the forward: 32 (fewer lanes per row, so fewer merge levels: the
+// forward is issue-bound), or the padded row when E <= 16.  Measured on B200 at 131072 rows
+// against 8 per lane: E=64,k=2 1.33x, E=128,k=8 1.97x, E=256,k=4 1.88x faster.  With too
+// few rows to give every SM a CTA of 256 threads at 32 per lane, 8 per lane keeps more
+// lanes busy (4096 x 64 rows: 1.9 us against 2.8 us).
+inline int fwd_elems(int E, int64_t rows) {
+  if (E <= 8) return 8;
+  if (E <= 16) return 16;
+  const int64_t lanes32 = rows * (int64_t)((E + 31) / 32);
+  return lanes32 < (int64_t)num_sms() * 256 ? 8 : 32;
+}
 constexpr int kLaneMaxKP = 8;   // largest list kept per lane
 
 __device__ __forceinline__ int skey(float x) {
@@ -330,12 +341,11 @@ __device__ __forceinline__ void merge_xor(int (&kv)[KP], int (&ki)[KP], int d) {
   }
 }
 
-template <typename T, int G, bool VEC>
+template <typename T, int G, int C, bool VEC>
 __device__ __forceinline__ void lanes_load(const T* __restrict__ logits, int64_t row_stride,
-                                           int64_t row, bool ok, int E, int l,
-                                           float (&x)[kLaneElems]) {
+                                           int64_t row, bool ok, int E, int l, float (&x)[C]) {
   constexpr int VN = 16 / (int)sizeof(T);
-  constexpr int P = kLaneElems / VN;
+  constexpr int P = C / VN;
   const T* rp = logits + row * row_stride;
 #pragma unroll
   for (int p = 0; p < P; ++p) {
@@ -357,13 +367,13 @@ __device__ __forceinline__ void lanes_load(const T* __restrict__ logits, int64_t
   }
 }
 
-template <typename T, int G, int KP, bool VEC>
+template <typename T, int G, int C, int KP, bool VEC>
 __global__ void __launch_bounds__(256) router_fwd_lanes(const T* __restrict__ logits,
                                                         int64_t row_stride, int64_t n_rows,
                                                         int E, int k, float* __restrict__ w_out,
                                                         int64_t* __restrict__ idx_out) {
   constexpr int VN = 16 / (int)sizeof(T);
-  constexpr int P = kLaneElems / VN;
+  constexpr int P = C / VN;
   constexpr int RPW = 32 / G;  // rows per warp per pass
   const int lane = threadIdx.x & 31;
   const int l = lane % G;
@@ -372,21 +382,22 @@ __global__ void __launch_bounds__(256) router_fwd_lanes(const T* __restrict__ lo
   const int64_t n_warps = ((int64_t)gridDim.x * blockDim.x) >> 5;
   const int64_t n_tiles = (n_rows + RPW - 1) / RPW;
 
-  float cur[kLaneElems];
+  float cur[C];
   {
     const int64_t row = warp_global * RPW + grp;
-    lanes_load<T, G, VEC>(logits, row_stride, row, warp_global < n_tiles && row < n_rows, E, l,
-                          cur);
+    lanes_load<T, G, C, VEC>(logits, row_stride, row, warp_global < n_tiles && row < n_rows, E,
+                             l, cur);
   }
   // The tile loop is warp-uniform: every lane reaches every shuffle.
   for (int64_t tile = warp_global; tile < n_tiles; tile += n_warps) {
     const int64_t row = tile * RPW + grp;
     const bool row_ok = row < n_rows;
-    float nxt[kLaneElems];
+    float nxt[C];
     {
       const int64_t nt = tile + n_warps;
       const int64_t nrow = nt * RPW + grp;
-      lanes_load<T, G, VEC>(logits, row_stride, nrow, nt < n_tiles && nrow < n_rows, E, l, nxt);
+      lanes_load<T, G, C, VEC>(logits, row_stride, nrow, nt < n_tiles && nrow < n_rows, E, l,
+                               nxt);
     }
     int kv[KP], ki[KP];
 #pragma unroll
@@ -433,7 +444,7 @@ __global__ void __launch_bounds__(256) router_fwd_lanes(const T* __restrict__ lo
       }
     }
 #pragma unroll
-    for (int i = 0; i < kLaneElems; ++i) cur[i] = nxt[i];
+    for (int i = 0; i < C; ++i) cur[i] = nxt[i];
   }
 }
 
@@ -585,8 +596,8 @@ int launch_full(const T* lp, int64_t rs, int64_t n, int E, int k, float* w, int6
   return FK_OK;
 }
 
-inline int lanes_per_row(int E) {
-  const int g = pow2_at_least((E + kLaneElems - 1) / kLaneElems);
+inline int lanes_per_row(int E, int elems) {
+  const int g = pow2_at_least((E + elems - 1) / elems);
   return g > 32 ? 32 : g;
 }
 
@@ -607,15 +618,15 @@ int resident_grid(K kernel, int64_t n_warp_tiles) {
   return (int)(ctas < 1 ? 1 : ctas);
 }
 
-template <typename T, int G, int KP>
+template <typename T, int G, int C, int KP>
 void launch_lanes_fwd(const T* lp, int64_t rs, int64_t n, int E, int k, float* w, int64_t* idx,
                       bool vec, cudaStream_t st) {
   const int64_t tiles = (n + 32 / G - 1) / (32 / G);
   if (vec) {
-    auto* kern = router_fwd_lanes<T, G, KP, true>;
+    auto* kern = router_fwd_lanes<T, G, C, KP, true>;
     kern<<<resident_grid(kern, tiles), 256, 0, st>>>(lp, rs, n, E, k, w, idx);
   } else {
-    auto* kern = router_fwd_lanes<T, G, KP, false>;
+    auto* kern = router_fwd_lanes<T, G, C, KP, false>;
     kern<<<resident_grid(kern, tiles), 256, 0, st>>>(lp, rs, n, E, k, w, idx);
   }
 }
@@ -623,13 +634,25 @@ void launch_lanes_fwd(const T* lp, int64_t rs, int64_t n, int E, int k, float* w
 template <typename T, int KP>
 void lanes_fwd_g(const T* lp, int64_t rs, int64_t n, int E, int k, float* w, int64_t* idx,
                  bool vec, cudaStream_t st) {
-  switch (lanes_per_row(E)) {
-    case 1: launch_lanes_fwd<T, 1, KP>(lp, rs, n, E, k, w, idx, vec, st); break;
-    case 2: launch_lanes_fwd<T, 2, KP>(lp, rs, n, E, k, w, idx, vec, st); break;
-    case 4: launch_lanes_fwd<T, 4, KP>(lp, rs, n, E, k, w, idx, vec, st); break;
-    case 8: launch_lanes_fwd<T, 8, KP>(lp, rs, n, E, k, w, idx, vec, st); break;
-    case 16: launch_lanes_fwd<T, 16, KP>(lp, rs, n, E, k, w, idx, vec, st); break;
-    default: launch_lanes_fwd<T, 32, KP>(lp, rs, n, E, k, w, idx, vec, st); break;
+  const int C = fwd_elems(E, n);
+  if (C == 8) {
+    switch (lanes_per_row(E, 8)) {
+      case 1: launch_lanes_fwd<T, 1, 8, KP>(lp, rs, n, E, k, w, idx, vec, st); break;
+      case 2: launch_lanes_fwd<T, 2, 8, KP>(lp, rs, n, E, k, w, idx, vec, st); break;
+      case 4: launch_lanes_fwd<T, 4, 8, KP>(lp, rs, n, E, k, w, idx, vec, st); break;
+      case 8: launch_lanes_fwd<T, 8, 8, KP>(lp, rs, n, E, k, w, idx, vec, st); break;
+      case 16: launch_lanes_fwd<T, 16, 8, KP>(lp, rs, n, E, k, w, idx, vec, st); break;
+      default: launch_lanes_fwd<T, 32, 8, KP>(lp, rs, n, E, k, w, idx, vec, st); break;
+    }
+  } else if (C == 16) {
+    launch_lanes_fwd<T, 1, 16, KP>(lp, rs, n, E, k, w, idx, vec, st);
+  } else {
+    switch (lanes_per_row(E, 32)) {  // E <= 256: at most 8 lanes
+      case 1: launch_lanes_fwd<T, 1, 32, KP>(lp, rs, n, E, k, w, idx, vec, st); break;
+      case 2: launch_lanes_fwd<T, 2, 32, KP>(lp, rs, n, E, k, w, idx, vec, st); break;
+      case 4: launch_lanes_fwd<T, 4, 32, KP>(lp, rs, n, E, k, w, idx, vec, st); break;
+      default: launch_lanes_fwd<T, 8, 32, KP>(lp, rs, n, E, k, w, idx, vec, st); break;
+    }
   }
 }
 
@@ -638,9 +661,8 @@ int fwd_t(const void* logits, int64_t rs, int64_t n, int E, int k, float* w, int
           cudaStream_t st) {
   const T* lp = static_cast<const T*>(logits);
   const int KPL = pow2_at_least(k);
-  // Measured on B200: the lane groups win for every k <= 8 up to E = 128; at 256 experts
-  // with k > 4 the 32-lane insertion chains lose to the segment network.
-  if (KPL <= kLaneMaxKP && !(KPL > 4 && lanes_per_row(E) == 32)) {
+  // Measured on B200: the lane groups win over the segment network for every k <= 8.
+  if (KPL <= kLaneMaxKP) {
     constexpr int VN = 16 / (int)sizeof(T);
     const bool vec = aligned16(logits) && (rs * (int64_t)sizeof(T)) % 16 == 0 && E % VN == 0;
     switch (KPL) {
@@ -713,7 +735,7 @@ extern "C" int fk_router_bwd(const float* dw, const float* w, const int64_t* idx
   // Every lane reads all k slots of its row, so the lane groups are used for k <= 4 only
   // (measured on B200: faster than the warp-per-row kernel there, slower at k = 8).
   if (KPL <= 4) {
-    const int G = fk::lanes_per_row(n_experts);
+    const int G = fk::lanes_per_row(n_experts, fk::kLaneElems);
     const bool vec = fk::aligned16(dlogits) && n_experts % 4 == 0;
     const int64_t tiles = (n_rows + 32 / G - 1) / (32 / G);
 #define FK_LANES(G_, KP_)                                                                  \
