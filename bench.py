@@ -384,7 +384,7 @@ class CrossEntropy(Workload):
         self.fwd()
         self.bwd()
 
-    launches_per_step = 4  # prologue, cluster kernel, finalize, backward scale (early exit)
+    launches_per_step = 4  # prologue, row kernel, finalize, backward scale (early exit)
 
     def units_per_step(self):
         return self.bytes / 1e9
@@ -638,7 +638,18 @@ class MoELayer(Workload):
         if self.world > 1:
             self.layer.allreduce_router_grad()  # data-parallel replicated router weight
 
-    launches_per_step = 17  # meta(2) gather up down combine | combine_bwd 2 dgrad 2 wgrad combine, router fwd/bwd
+    @property
+    def launches_per_step(self):
+        """Kernels of this library per step.  One GPU: router fwd/bwd 2, metadata 2,
+        gather, up, down, combine | combine_bwd, 2 dgrad, 2 wgrad, combine = 14.
+        Expert parallel (peer transport): router 2, plan 2, 2 puts, 4 waits, metadata 2,
+        gather, up, down, 2 combine-puts, 2 unpack sums, unpack dw, combine_bwd, 2 dgrad,
+        2 wgrad (4 when experts are replicated) = 25 (27); NCCL transport: 2 packs and the
+        local combines instead of the puts, waits and combine-puts = 21 (23)."""
+        if self.world == 1:
+            return 14
+        base = 25 if self.ep_transport == "peer" else 21
+        return base + (2 if self.replicated else 0)
 
     def units_per_step(self):
         return self.tokens
