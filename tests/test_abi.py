@@ -68,3 +68,24 @@ def test_ce_rejects_bad_smoothing():
     st = lib.fk_ce_fwd(None, 4, None, 4, None, 0, 4, -100, 1.5, 0, None, ctypes.byref(f),
                        ctypes.byref(one), ctypes.byref(one), None)
     assert st == 1
+
+
+def test_ep_planning_workspace_and_peer_argument_checks():
+    """The expert-parallel entry points validate their arguments on the host (no device
+    work happens for a rejected call)."""
+    lib = _lib.load()
+    n = ctypes.c_size_t(0)
+    assert lib.fk_ep_plan_workspace_size(1000, 8, ctypes.byref(n)) == 0
+    assert n.value == 4 * 8 * 4  # ceil(1000 / 256) chunks x 8 ranks x int32
+    assert lib.fk_ep_plan_workspace_size(10, 33, ctypes.byref(n)) == 1  # at most 32 ranks
+    # n_ranks 0, my_rank out of range, phase out of range
+    assert lib.fk_ep_peer_put_rows(None, 64, None, 4, 0, 0, None, None, 2, None, None, None,
+                                   None, 0, None, 2, None) == 1
+    assert lib.fk_ep_peer_put_rows(None, 64, None, 4, 2, 2, None, None, 2, None, None, None,
+                                   None, 0, None, 2, None) == 1
+    assert lib.fk_ep_peer_combine_put(None, 64, None, None, 4, 2, 0, 2, None, None, None, None,
+                                      4, None, 2, None) == 1
+    assert lib.fk_ep_peer_wait(None, 2, 0, None, 100, None, None) == 1
+    assert lib.fk_ep_peer_wait(None, 0, 0, None, 100, None, None) == 1
+    assert lib.fk_ipc_alloc(0, None, None) == 1
+    assert lib.fk_ipc_open(None, None) == 1
