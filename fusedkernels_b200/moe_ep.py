@@ -1,21 +1,28 @@
-"""Expert-parallel sorted-dispatch MoE layer (one process per GPU, NCCL over NVLink).
+"""Expert-parallel sorted-dispatch MoE layer (one process per GPU on one node).
 
 The reference runs every expert on one GPU (fusedkernels/moe_layer_sorted.py:37); this
 module shards the experts of ``FusedMoEMLPSorted`` across the ranks of a process group
-(16 experts per GPU for E=128 on 8 GPUs) and exchanges token rows with all-to-all:
+(16 experts per GPU for E=128 on 8 GPUs) and exchanges token rows between them:
 
   forward   route locally -> fk_ep_plan (which ranks need each token, deduplicated) ->
-            fk_ep_pack -> all-to-all of rows and slot metadata -> local grouped-GEMM
-            experts on the received rows -> per-row pre-reduction of the local slots ->
-            all-to-all back -> fk_ep_unpack_sum (rank-ordered sum: deterministic)
+            rows and slot metadata to the expert ranks -> local grouped-GEMM experts on
+            the received rows -> per-row pre-reduction of the local slots -> partial rows
+            back -> fk_ep_unpack_sum (rank-ordered sum: deterministic)
   backward  the mirror image: dout rows out, per-slot routing gradients and partial input
-            gradients back; the input-gradient all-to-all runs concurrently with the
-            weight-gradient GEMMs.
+            gradients back; the return exchange overlaps the weight-gradient GEMMs.
 
 Every (source, destination) pair has a fixed capacity of T rows (a token is sent at most
-once per destination), so all collectives have static sizes: no host synchronisation and
-no split-size exchange.  Expert placement is static and load-aware: ``lpt_placement``
-bin-packs experts, hottest first, onto the least-loaded rank with a free slot.
+once per destination), so no host synchronisation or split-size exchange is needed.
+
+Transports: ``"peer"`` (default) -- put kernels store the rows straight into the other
+ranks' memory over NVLink (``PeerExchange``, csrc/moe_ep_peer.cu); ``"nccl"`` --
+fk_ep_pack + fixed-capacity ``all_to_all_single``.
+
+Placement is static and load-aware: ``lpt_placement`` bin-packs experts, hottest first,
+onto the least-loaded rank with a free slot.  Experts hot enough that nearly every token
+picks them (``hot_experts``) can be replicated on every rank instead: their slots are
+computed on the token's own rank and their weight gradients are summed over the group
+inside backward (``lpt_placement_excluding`` places the rest).
 
 ``ExpertParallelMoEMLP`` keeps the reference's parameter naming for the experts it holds
 (``experts.<global id>.w_gate.weight`` ...) and a replicated ``router``.  Gradients of the
