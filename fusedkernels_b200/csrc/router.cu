@@ -605,13 +605,13 @@ inline int lanes_per_row(int E, int elems) {
 // SM runs a second partial wave (the kernels are register-limited below 8 CTAs per SM).
 template <typename K>
 int resident_grid(K kernel, int64_t n_warp_tiles) {
-  static int per_sm = 0;  // one cached value per kernel instantiation
-  if (per_sm == 0) {
+  // one value per kernel instantiation, computed once (thread-safe static initialisation)
+  static const int per_sm = [kernel] {
     int b = 0;
     if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, kernel, 256, 0) != cudaSuccess || b < 1)
       b = 1;
-    per_sm = b;
-  }
+    return b;
+  }();
   int64_t ctas = (n_warp_tiles + 7) / 8;
   const int64_t cap = (int64_t)num_sms() * per_sm;
   if (ctas > cap) ctas = cap;
