@@ -427,7 +427,7 @@ __global__ void __launch_bounds__(kRowThreads, 1) ce_row_kernel(
   }
 }
 
-// Fallback for rows longer than the cluster path holds: one CTA per row, three sweeps.
+// Fallback for rows that are not 16-byte aligned: one CTA per row, three scalar sweeps.
 template <typename T>
 __global__ void __launch_bounds__(kCeThreads) ce_generic_kernel(
     const T* __restrict__ logits, int64_t lstride, T* grad, int64_t gstride,
