@@ -1,6 +1,11 @@
 // RMSNorm forward/backward (fp32 accumulation, reference rmsnorm.py:20-71).
 //
-// Register path (the fast one): persistent CTAs walk rows r = blockIdx.x, += gridDim.x.
+// Path selection for 16-byte aligned rows (the workloads): rows of at most 4 KB use the
+// forward warp rings, rows of at most 16 KB the TMA ring kernels (shared-memory rings
+// filled by cp.async.bulk, below), longer rows the register path; unaligned rows the
+// generic path.  All share the row walk, the fixed-order reductions and the dw scheme.
+//
+// Register path: persistent CTAs walk rows r = blockIdx.x, += gridDim.x.
 // A CTA of T threads covers one row with VPT 16-byte packets per thread; the packet
 // index of (thread t, slot j) is j*T + t, so every slot is one fully coalesced sweep of
 // the row.  The weight slice a thread needs is loaded once into registers and reused
