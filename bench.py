@@ -499,13 +499,13 @@ class Router(Workload):
         dw = self.dw_h
         reps, t0 = 0, time.perf_counter()
         while True:
-            route_oracle(lg, self.k)
-            route_bwd_oracle(lg, self.k, dw)
+            _, idx = route_oracle(lg, self.k, torch.float32)
+            route_bwd_oracle(lg, self.k, dw, torch.float32, idx)
             reps += 1
             if time.perf_counter() - t0 > 8.0:
                 break
         dt = (time.perf_counter() - t0) / reps
-        return dt, self.rows, f"all {self.rows} rows, fp64 stable-sort router fwd+bwd, {reps} reps"
+        return dt, self.rows, f"all {self.rows} rows, fp32 stable-sort router fwd+bwd, {reps} reps"
 
     def config(self):
         return {"workload": "moe_router_fwd_bwd", "shape": [self.rows, self.E], "k": self.k,
@@ -1030,10 +1030,10 @@ def wl_setup_host(wl):
         def once():
             from oracle import route_bwd_oracle, route_oracle
             t0 = time.perf_counter()
-            route_oracle(lg, wl.k)
-            route_bwd_oracle(lg, wl.k, dw)
+            _, idx = route_oracle(lg, wl.k, torch.float32)
+            route_bwd_oracle(lg, wl.k, dw, torch.float32, idx)
             return time.perf_counter() - t0, wl.rows, \
-                f"all {wl.rows} rows per step, fp64 stable-sort router fwd+bwd"
+                f"all {wl.rows} rows per step, fp32 stable-sort router fwd+bwd"
     else:
         raise ValueError(wl)
     wl.cpu_sample_once = once

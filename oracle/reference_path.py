@@ -13,7 +13,7 @@ import torch.nn.functional as F
 
 
 # ------------------------------------------------------------------------ router -------
-def route_oracle(logits: torch.Tensor, k: int):
+def route_oracle(logits: torch.Tensor, k: int, dtype=torch.float64):
     """Top-k router: softmax over E, top-k by logit, renormalise.
 
     Restates ``naive_route`` (tests/test_moe_routing_v2.py:11-15) -- softmax, topk,
@@ -24,9 +24,11 @@ def route_oracle(logits: torch.Tensor, k: int):
     an fp64 softmax and renormalised (moe_routing_v2.py:48-94 computes the same
     quantities: probs, gather at the selected indices, divide by their sum).
 
-    Returns (w float32 [N, k], idx int64 [N, k]) in descending rank order.
+    Returns (w float32 [N, k], idx int64 [N, k]) in descending rank order.  ``dtype`` is
+    the arithmetic precision (fp64 for parity; fp32, the reference path's own, for the
+    timed CPU baseline).
     """
-    x = logits.detach().to(torch.float64).cpu()
+    x = logits.detach().to(dtype).cpu()
     key = torch.where(x == 0, torch.zeros_like(x), x)  # fold -0.0 onto +0.0
     idx = torch.sort(key, dim=-1, descending=True, stable=True).indices[:, :k]
     probs = torch.softmax(x, dim=-1)
@@ -35,20 +37,23 @@ def route_oracle(logits: torch.Tensor, k: int):
     return w.to(torch.float32), idx
 
 
-def route_bwd_oracle(logits: torch.Tensor, k: int, dw: torch.Tensor) -> torch.Tensor:
+def route_bwd_oracle(logits: torch.Tensor, k: int, dw: torch.Tensor, dtype=torch.float64,
+                     idx: torch.Tensor | None = None) -> torch.Tensor:
     """dlogits for upstream dw at fixed selection (moe_routing_v2.py:102-126).
 
     The selection is not differentiated (moe_routing_v2.py:109-112); the renormalised
     weights are a softmax over the selected logits, so autograd through
     softmax -> gather -> renormalise gives w_j (dw_j - sum_m w_m dw_m) at the selected
-    columns and exactly 0 elsewhere.  fp64, returned as fp32.
+    columns and exactly 0 elsewhere.  fp64 by default, returned as fp32; ``idx`` reuses a
+    selection already made by ``route_oracle``.
     """
-    x = logits.detach().to(torch.float64).cpu().requires_grad_(True)
-    _, idx = route_oracle(logits, k)
+    x = logits.detach().to(dtype).cpu().requires_grad_(True)
+    if idx is None:
+        _, idx = route_oracle(logits, k, dtype)
     probs = torch.softmax(x, dim=-1)
     w = torch.gather(probs, 1, idx)
     w = w / w.sum(dim=-1, keepdim=True)
-    w.backward(dw.detach().to(torch.float64).cpu())
+    w.backward(dw.detach().to(dtype).cpu())
     return x.grad.to(torch.float32)
 
 
