@@ -3,7 +3,10 @@
  *
  * Every entry point takes raw device pointers, explicit sizes/strides and a CUDA stream
  * (passed as `void*`, i.e. a cudaStream_t / CUstream; NULL = legacy default stream).
- * All buffers are owned by the caller; no entry point allocates device memory.
+ * All buffers are owned by the caller.  Two exceptions allocate or hold device memory:
+ * fk_ipc_alloc (the expert-parallel exchange region) calls cudaMalloc, and
+ * fk_rmsnorm_bwd_noalloc keeps its scratch in a module-global device array that the
+ * driver creates when the library's device code is first loaded on a device.
  * Work is enqueued asynchronously on `stream`; the return value only reports argument
  * and launch errors (FK_OK == 0).  Device-side data errors (e.g. an out-of-range
  * cross-entropy target) are reported through a caller-provided int flag in device memory.
@@ -87,8 +90,14 @@ FK_API int fk_rmsnorm_bwd(const void* dy, const void* x, const void* weight, int
  * The weight-gradient partials go to one fixed 8 MiB device array inside the library, which
  * every GPU that loads the library keeps until the process exits; cols must be at most
  * 2,097,152 (one fp32 partial row), larger cols are rejected with FK_ERR_UNSUPPORTED.
- * The first call on a device looks the array's device address up (cudaGetSymbolAddress);
- * make that first call before any CUDA stream capture.  Every call uses the same array:
+ * Under CUDA's lazy module loading (the default since CUDA 12.2) the array is created on a
+ * device when the library's device code is first loaded there, at the latest on the first
+ * call, not when the library is opened: a caller with a fixed memory budget makes one call
+ * during its set-up, before it plans the rest of its memory.
+ * The first call on a device looks the array's device address up (cudaGetSymbolAddress)
+ * and keeps it for the life of the process; make that first call before any CUDA stream
+ * capture.  The kept address is not valid after cudaDeviceReset on that device: do not
+ * call this entry point after a device reset in the same process.  Every call uses the same array:
  * calls that may run at the same time on the GPU (different streams, or different host
  * threads on one device) race on it and must be serialised by the caller.
  * Allocates nothing: no cudaMalloc/cudaFree and no allocating library call. */

@@ -33,3 +33,12 @@ def golden():
 
 def gen(seed: int) -> torch.Generator:
     return torch.Generator().manual_seed(seed)
+
+
+@pytest.fixture(scope="session")
+def golden_moe():
+    """Outputs of the reference's NaiveMoEMLP (tests/golden/make_moe_golden.py)."""
+    import numpy as np
+    path = os.path.join(ROOT, "tests", "golden", "golden_moe.npz")
+    with np.load(path) as z:
+        return {k: z[k] for k in z.files}

@@ -5,7 +5,7 @@ autograd wrappers assert ``is_cuda``, so this script calls the ``@triton.jit`` k
 directly, with the launch arguments the wrappers use, under ``TRITON_INTERPRET=1``
 (Triton's CPU interpreter).  Outputs are stored with their inputs in ``golden.npz``.
 
-    python tests/golden/make_golden.py [path-to-reference-checkout]
+    python tests/golden/make_golden.py <path-to-reference-checkout>
 
 Only this generator reads the reference checkout; the tests read ``golden.npz``.
 """
@@ -13,7 +13,9 @@ import os
 import sys
 
 os.environ["TRITON_INTERPRET"] = "1"
-REF = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+if len(sys.argv) != 2:
+    sys.exit("usage: python tests/golden/make_golden.py <path-to-reference-checkout>")
+REF = sys.argv[1]
 sys.path.insert(0, REF)
 
 import numpy as np  # noqa: E402

@@ -59,3 +59,28 @@ def test_router_oracle_tie_break_lower_index():
     nan_row = torch.tensor([[0.5, float("nan"), float("inf"), 1.0]])
     _, idx = route_oracle(nan_row, 3)
     assert idx.tolist() == [[1, 2, 3]]
+
+
+MOE_TAGS = ("e8k2", "e32k4", "e64k8", "e128k16", "empty")
+
+
+def test_moe_layer_oracle_matches_reference_naive_layer(golden_moe):
+    """moe_layer_oracle against the reference's own NaiveMoEMLP (fp64 on the CPU, stored as
+    fp32): forward output, input gradient (expert and router paths), router weight
+    gradient and every expert's weight gradients; atol 1e-6 / rtol 1e-5."""
+    from oracle import moe_layer_oracle
+    tol = dict(atol=1e-6, rtol=1e-5)
+    for tag in MOE_TAGS:
+        g = {k[len(f"moe_{tag}_"):]: v for k, v in golden_moe.items() if k.startswith(f"moe_{tag}_")}
+        x, wr = T(g["x"]).double(), T(g["wr"]).double()
+        logits = x @ wr.t()
+        out, dx, dwg, dwu, dwd, dl = moe_layer_oracle(x, logits, T(g["wg"]), T(g["wu"]), T(g["wd"]),
+                                                      int(g["k"]), T(g["dout"]))
+        torch.testing.assert_close(out.float(), T(g["out"]), **tol, msg=tag)
+        torch.testing.assert_close((dx + dl @ wr).float(), T(g["dx"]), **tol, msg=tag)
+        torch.testing.assert_close((dl.t() @ x).float(), T(g["dwr"]), **tol, msg=tag)
+        torch.testing.assert_close(dwg.float(), T(g["dwg"]), **tol, msg=tag)
+        torch.testing.assert_close(dwu.float(), T(g["dwu"]), **tol, msg=tag)
+        torch.testing.assert_close(dwd.float(), T(g["dwd"]), **tol, msg=tag)
+    # the many-experts case leaves experts without tokens: their gradients are exactly 0
+    assert (T(golden_moe["moe_empty_dwg"]).flatten(1).abs().sum(1) == 0).sum() >= 56

@@ -46,8 +46,12 @@ def _no_alloc(x, dy, w, rstd):
     return dx, dw
 
 
+# 4096 x 16384 bf16 and 1024 x 65536 fp32 need more partial rows than the fixed scratch
+# holds (128 and 32 fit), so the grid is capped below one CTA per SM there.
 @pytest.mark.parametrize("rows,cols,dtype", [(4096, 4096, torch.bfloat16), (1000, 1024, torch.float16),
-                                             (300, 301, torch.float32), (7, 40000, torch.float32)])
+                                             (300, 301, torch.float32), (7, 40000, torch.float32),
+                                             (4096, 16384, torch.bfloat16),
+                                             (1024, 65536, torch.float32)])
 def test_no_alloc_matches_workspace_entry_point_twice(rows, cols, dtype):
     x, dy, w, rstd = _inputs(rows, cols, dtype, rows + cols)
     ref_dx, ref_dw = _with_workspace(x, dy, w, rstd)
