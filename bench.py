@@ -1,15 +1,20 @@
 """Benchmark of the fusedkernels hot path on B200.
 
-    python bench.py [--workload rmsnorm|swiglu|ce|router|moe] [--gpus N] [--steps K]
+    python bench.py [--workload moe|rmsnorm|swiglu|ce|router] [--gpus N] [--steps K]
                     [--warmup W] [--impl ours|reference]
+
+The default workload is the sorted-dispatch MoE layer (x [32768, 4096] bf16, E=128, k=8,
+hidden 1024): one GPU runs the whole layer, N GPUs run it expert-parallel over NVLink.
 
 One JSON line on rank 0.  A step is one forward+backward pass of the workload's op over
 one batch of seeded synthetic input at the workload's full shape.  ``value`` is timed on
 the device (CUDA events, inputs resident in HBM, outputs preallocated, the kernels called
 through the C ABI); ``e2e`` times the same step through the public Python API with the
-step's inputs copied from pinned host memory and its result read back inside the timed
-region.  With N ranks (torchrun) every rank runs its own batch (weak scaling: rows shard
-with no exchange) and ``value`` aggregates all ranks over the slowest rank's time.
+step's inputs copied from pinned host memory and every result (outputs and all gradients)
+copied back to pinned host memory inside the timed region.  With N ranks (torchrun) the
+MoE layer splits its 32768 tokens over the ranks and shards the experts (strong scaling,
+token rows exchanged over NVLink); the row ops run one batch per rank (weak scaling: rows
+shard with no exchange).  ``value`` aggregates all ranks over the slowest rank's time.
 
 ``--impl reference`` times the reference path's CPU implementation (the oracle in
 oracle/, all host threads) on a bounded sample of the same workload; only rank 0 runs.
@@ -128,6 +133,28 @@ def gen(seed):
     return torch.Generator().manual_seed(seed)
 
 
+class PinnedSink:
+    """Pinned host destinations for a step's device results.  ``put`` enqueues an async
+    device-to-host copy on the current stream (so it is inside the CUDA-event timed region)
+    and counts its bytes; buffers are allocated on first use and reused."""
+
+    def __init__(self):
+        self.bufs = {}
+        self.nbytes = 0
+
+    def start(self):
+        self.nbytes = 0
+
+    def put(self, key, t):
+        t = t.detach()
+        b = self.bufs.get(key)
+        if b is None or b.shape != t.shape or b.dtype != t.dtype:
+            b = torch.empty(t.shape, dtype=t.dtype, pin_memory=True)
+            self.bufs[key] = b
+        b.copy_(t, non_blocking=True)
+        self.nbytes += t.numel() * t.element_size()
+
+
 def cur_stream():
     return torch.cuda.current_stream().cuda_stream
 
@@ -222,17 +249,22 @@ class RMSNorm(Workload):
         self.norm = fk.FusedRMSNorm(self.cols, eps=1e-6).to(self.dev)
         with torch.no_grad():
             self.norm.weight.copy_(self.w)
+        self.sink = PinnedSink()
 
     def e2e_step(self):
+        """x, dy in; every result (y, dx, dw) back to pinned host memory."""
+        self.sink.start()
         x = self.x_h.to(self.dev, non_blocking=True).requires_grad_(True)
         dy = self.dy_h.to(self.dev, non_blocking=True)
         self.norm.weight.grad = None
         y = self.norm(x)
         y.backward(dy)
-        return self.norm.weight.grad.to("cpu", non_blocking=True)
+        self.sink.put("y", y)
+        self.sink.put("dx", x.grad)
+        self.sink.put("dw", self.norm.weight.grad)
 
     def e2e_bytes(self):
-        return self.x_h.numel() * 2 * 2, self.cols * 4
+        return self.x_h.numel() * 2 * 2, self.sink.nbytes
 
     def cpu_sample(self):
         """Oracle (RefRMSNorm, fp32) on 512 rows x 4096; returns (seconds, GB of work)."""
@@ -307,19 +339,23 @@ class SwiGLU(Workload):
         return [("swiglu_bwd", self.bwd, self.bwd_bytes), ("swiglu_fwd", self.fwd, self.fwd_bytes)]
 
     def e2e_setup(self):
-        pass
+        self.sink = PinnedSink()
 
     def e2e_step(self):
+        """gate, up, dout in; out, dgate, dup back to pinned host memory."""
         import fusedkernels_b200 as fk
+        self.sink.start()
         g = self.g_h.to(self.dev, non_blocking=True).requires_grad_(True)
         u = self.u_h.to(self.dev, non_blocking=True).requires_grad_(True)
         d = self.d_h.to(self.dev, non_blocking=True)
         out = fk.fused_swiglu(g, u)
         out.backward(d)
-        return g.grad[0, :8].to("cpu", non_blocking=True)
+        self.sink.put("out", out)
+        self.sink.put("dg", g.grad)
+        self.sink.put("du", u.grad)
 
     def e2e_bytes(self):
-        return self.n * 2 * 3, 16
+        return self.n * 2 * 3, self.sink.nbytes
 
     def cpu_sample(self):
         from oracle import swiglu_oracle
@@ -393,18 +429,21 @@ class CrossEntropy(Workload):
         return [("ce_fwd", self.fwd, self.bytes)]
 
     def e2e_setup(self):
-        pass
+        self.sink = PinnedSink()
 
     def e2e_step(self):
+        """logits, targets in; the loss and the full logits gradient back to pinned host."""
         import fusedkernels_b200 as fk
+        self.sink.start()
         x = self.x_h.to(self.dev, non_blocking=True).requires_grad_(True)
         t = self.t_h.to(self.dev, non_blocking=True)
         loss = fk.fused_cross_entropy(x, t, inplace_grad=True)
         loss.backward()
-        return loss.detach().to("cpu", non_blocking=True)
+        self.sink.put("loss", loss)
+        self.sink.put("grad", x.grad)
 
     def e2e_bytes(self):
-        return self.rows * self.cols * 2 + self.rows * 8, 4
+        return self.rows * self.cols * 2 + self.rows * 8, self.sink.nbytes
 
     def cpu_sample(self):
         from oracle import cross_entropy_oracle
@@ -480,18 +519,22 @@ class Router(Workload):
         return [("router_fwd", self.fwd, self.fwd_bytes), ("router_bwd", self.bwd, self.bwd_bytes)]
 
     def e2e_setup(self):
-        pass
+        self.sink = PinnedSink()
 
     def e2e_step(self):
+        """logits, dw in; weights, indices and dlogits back to pinned host memory."""
         import fusedkernels_b200 as fk
+        self.sink.start()
         lg = self.l_h.to(self.dev, non_blocking=True).requires_grad_(True)
         dw = self.dw_h.to(self.dev, non_blocking=True)
         w, idx = fk.fused_moe_route_v2(lg, self.k)
         w.backward(dw)
-        return lg.grad.to("cpu", non_blocking=True)
+        self.sink.put("w", w)
+        self.sink.put("idx", idx)
+        self.sink.put("dl", lg.grad)
 
     def e2e_bytes(self):
-        return self.rows * (self.E + self.k) * 4, self.rows * self.E * 4
+        return self.rows * (self.E + self.k) * 4, self.sink.nbytes
 
     def cpu_sample(self):
         from oracle import route_bwd_oracle, route_oracle
@@ -528,6 +571,7 @@ class MoELayer(Workload):
     name = "moe"
     metric = "MoE layer fwd+bwd throughput"
     ep_transport = "peer"
+    ep_replicate = "auto"
     unit = "tokens/s"
     strong = True  # the 32768 global tokens are split across ranks
     tokens, dim, hidden, E, k = 32768, 4096, 1024, 128, 8
@@ -564,13 +608,17 @@ class MoELayer(Workload):
         else:
             from fusedkernels_b200.moe_ep import (ExpertParallelMoEMLP, hot_experts,
                                                   lpt_placement_excluding)
-            # Load-aware static placement from the expert loads of this batch (computed
-            # identically on every rank from the same full batch: no communication).
+            # Load-aware static placement from the expert loads of a calibration batch
+            # (seed 1; the timed batch is seed 0), computed identically on every rank: no
+            # communication.
             with torch.no_grad():
-                logits = x_all.to(dev) @ wr.t() + bias
+                x_cal = torch.randn(self.tokens, D, generator=gen(1)).bfloat16().to(dev)
+                logits = x_cal @ wr.t() + bias
                 _, idx = fk.fused_moe_route_v2(logits, self.k)
                 load = torch.bincount(idx.reshape(-1), minlength=E).float().cpu()
-            self.replicated = hot_experts(load.tolist(), self.world)
+                del x_cal, logits
+            self.replicated = (hot_experts(load.tolist(), self.world)
+                               if self.ep_replicate == "auto" else [])
             self.placement = lpt_placement_excluding(load.tolist(), self.world, self.replicated)
             layer = ExpertParallelMoEMLP(D, H, E, self.k, placement=self.placement,
                                          transport=self.ep_transport,
@@ -662,9 +710,12 @@ class MoELayer(Workload):
                 ("moe_gemm_down", self.gemm_down, 2 * A * self.dim * self.hidden)]
 
     def e2e_setup(self):
-        pass
+        self.sink = PinnedSink()
 
     def e2e_step(self):
+        """x, dout in; out, dx, the router gradient and the gradient of every expert weight
+        this GPU holds back to pinned host memory."""
+        self.sink.start()
         self.layer.zero_grad(set_to_none=True)
         x = self.x_h.to(self.dev, non_blocking=True).requires_grad_(True)
         d = self.d_h.to(self.dev, non_blocking=True)
@@ -672,10 +723,14 @@ class MoELayer(Workload):
         out.backward(d)
         if self.world > 1:
             self.layer.allreduce_router_grad()
-        return self.layer.router.weight.grad.to("cpu", non_blocking=True)
+        self.sink.put("out", out)
+        self.sink.put("dx", x.grad)
+        for name, prm in self.layer.named_parameters():
+            if prm.grad is not None:
+                self.sink.put(name, prm.grad)
 
     def e2e_bytes(self):
-        return self.x_h.numel() * 2 * 2, self.E * self.dim * 2
+        return self.x_h.numel() * 2 * 2, self.sink.nbytes
 
     def cpu_sample(self):
         return moe_cpu_sample(self, 256)
@@ -684,7 +739,8 @@ class MoELayer(Workload):
         par = "single GPU" if self.world == 1 else (
             f"ep{self.world}: {len(self.replicated)} hot experts replicated on every GPU "
             f"(gradients all-reduced), the other {self.E - len(self.replicated)} placed by "
-            f"load-aware LPT bin packing, dispatch/combine "
+            f"load-aware LPT bin packing (placement and replicated set from a calibration "
+            f"batch, seed 1; the timed batch is seed 0), dispatch/combine "
             + ("by put kernels into peer memory over NVLink" if self.ep_transport == "peer"
                else "by NCCL all-to-all") + f"; {self.tokens // self.world} tokens per GPU")
         return {"workload": "moe_sorted_dispatch_fwd_bwd", "tokens": self.tokens, "dim": self.dim,
@@ -767,6 +823,7 @@ def run_ours(args):
         wl.rows = args.rows
     if args.workload == "moe":
         wl.ep_transport = args.ep_transport
+        wl.ep_replicate = args.ep_replicate
         if args.moe_tokens:
             wl.tokens = args.moe_tokens
         if args.moe_experts:
@@ -928,6 +985,7 @@ def run_breakdown(args, reps=5):
     wl = make_workload(args)
     if args.workload == "moe":
         wl.ep_transport = args.ep_transport
+        wl.ep_replicate = args.ep_replicate
     wl.setup(dev)
     for _ in range(max(args.warmup, 3)):
         wl.step()
@@ -1045,7 +1103,7 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="rmsnorm")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="moe")
     ap.add_argument("--router-rows", type=int, default=4096)
     ap.add_argument("--router-experts", type=int, default=64, help="profiling runs only")
     ap.add_argument("--router-k", type=int, default=2, help="profiling runs only")
@@ -1055,6 +1113,9 @@ def main():
                     help="override the row count of rmsnorm/swiglu/ce (profiling runs only)")
     ap.add_argument("--ep-transport", choices=["peer", "nccl"], default="peer",
                     help="token exchange of the expert-parallel MoE layer (N > 1)")
+    ap.add_argument("--ep-replicate", choices=["auto", "none"], default="auto",
+                    help="auto: replicate the experts hot enough that nearly every token picks "
+                         "them on every GPU; none: exactly E/N experts per GPU")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--breakdown", action="store_true",
                     help="print the device time of every C-ABI call in one step (eager, CUDA "

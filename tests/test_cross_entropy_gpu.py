@@ -167,3 +167,78 @@ def test_ce_full_size_properties():
     assert torch.count_nonzero(grad[ign]) == 0
     row_sums = grad[~ign].float().sum(-1) * n_valid
     assert row_sums.abs().max().item() < 0.05
+
+
+def test_global_mean_single_process_equals_local_mean():
+    """Without a process group the sharded-batch form is the plain fused loss."""
+    from fusedkernels_b200.cross_entropy import fused_cross_entropy_global_mean
+    G = gen(31)
+    x = (torch.randn(64, 3000, generator=G) * 2).bfloat16()
+    t = torch.randint(0, 3000, (64,), generator=G)
+    t[::4] = -100
+    a = x.cuda().requires_grad_(True)
+    la = fk.fused_cross_entropy(a, t.cuda())
+    la.backward(torch.tensor(0.5, device="cuda"))
+    b = x.cuda().requires_grad_(True)
+    lb = fused_cross_entropy_global_mean(b, t.cuda())
+    lb.backward(torch.tensor(0.5, device="cuda"))
+    torch.testing.assert_close(lb, la, atol=1e-6, rtol=1e-5)
+    torch.testing.assert_close(b.grad.float(), a.grad.float(), atol=1e-6, rtol=1e-2)
+
+
+def _ce_worker(rank, world, port, q):
+    import datetime
+    import os
+    import sys
+    import torch.distributed as dist
+    sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    from fusedkernels_b200.cross_entropy import fused_cross_entropy_global_mean
+    dev = torch.device("cuda", rank)
+    torch.cuda.set_device(dev)
+    try:
+        dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
+                                world_size=world, timeout=datetime.timedelta(seconds=60))
+        G = torch.Generator().manual_seed(41)
+        x = (torch.randn(256, 4096, generator=G) * 2).bfloat16()
+        t = torch.randint(0, 4096, (256,), generator=G)
+        t[::3] = -100
+        per = 256 // world
+        xs = x[rank * per:(rank + 1) * per].to(dev).requires_grad_(True)
+        loss = fused_cross_entropy_global_mean(xs, t[rank * per:(rank + 1) * per].to(dev))
+        loss.backward()
+        q.put((rank, float(loss), xs.grad.float().cpu()))
+    except Exception as exc:
+        q.put((rank, repr(exc), None))
+    finally:
+        if dist.is_initialized():
+            dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_global_mean_two_ranks_nccl():
+    """Two ranks, one half of the rows each: both see the full-batch mean loss, and each
+    rank's gradient equals its rows of the full-batch gradient."""
+    import socket
+    import torch.multiprocessing as mp
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_ce_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = sorted([q.get(timeout=180) for _ in procs], key=lambda r: r[0])
+    for p in procs:
+        p.join(timeout=60)
+    G = torch.Generator().manual_seed(41)
+    x = (torch.randn(256, 4096, generator=G) * 2).bfloat16()
+    t = torch.randint(0, 4096, (256,), generator=G)
+    t[::3] = -100
+    rl, rg = cross_entropy_oracle(x, t)
+    for rank, loss, grad in res:
+        assert not isinstance(loss, str), f"rank {rank}: {loss}"
+        assert abs(loss - float(rl)) <= 1e-4 * abs(float(rl))
+        ref = rg[rank * 128:(rank + 1) * 128].float()
+        torch.testing.assert_close(grad, ref.bfloat16().float(), atol=1e-6, rtol=1e-2)

@@ -288,9 +288,39 @@ def test_layer_state_dict_keys_and_error_flags():
     layer(x).float().sum().backward()
 
 
-def test_layer_workload_shape_sampled_tokens():
-    """x [32768, 4096] bf16, E=128, k=8, H=1024, Zipf(1.1) expert bias on the logits:
-    16 sampled tokens' outputs and input gradients vs a per-token fp64 evaluation."""
+def _token_reference(layer, x_t, dout_t, w, idx, H):
+    """fp64 forward output and input gradient of one token (expert and router paths)."""
+    ref = torch.zeros_like(x_t)
+    dx = torch.zeros_like(x_t)
+    ys, dacts = [], []
+    for j in range(idx.numel()):
+        e = int(idx[j])
+        h = layer.w13[e].double() @ x_t
+        g, u = h[:H], h[H:]
+        a = F.silu(g) * u
+        y = layer.w2[e].double() @ a
+        ys.append(y)
+        ref += float(w[j]) * y
+        dact = float(w[j]) * (layer.w2[e].double().t() @ dout_t)
+        s = torch.sigmoid(g)
+        dg = dact * u * s * (1 + g * (1 - s))
+        du = dact * g * s
+        dx += layer.w13[e, :H].double().t() @ dg + layer.w13[e, H:].double().t() @ du
+    # router path: d out / d w_j = dout . y_j; renormalised-softmax Jacobian at the selection
+    dw = torch.stack([dout_t @ y for y in ys])
+    wd = w.double().to(dout_t.device)
+    dl = wd * (dw - (wd * dw).sum())
+    dx += (dl[:, None] * layer.router.weight.double()[idx.to(dout_t.device)]).sum(0)
+    return ref, dx
+
+
+@pytest.mark.slow
+def test_layer_workload_shape_sampled_tokens_and_expert_gradients():
+    """x [32768, 4096] bf16, E=128, k=8, H=1024, Zipf(1.1) expert bias on the logits.
+    Forward outputs and input gradients of 16 sampled tokens against a per-token fp64
+    evaluation, and the weight gradients of the hottest expert (a ~30 K-token segment:
+    the long-K weight-gradient path of the timed step) and of two cold experts against fp32
+    matmuls over their token segments (bf16 inputs; 2e-2 of the tensor's max magnitude)."""
     torch.manual_seed(3)
     N, D, H, E, k = 32768, 4096, 1024, 128, 8
     layer = FusedMoEMLPSorted(D, H, E, k)
@@ -305,15 +335,52 @@ def test_layer_workload_shape_sampled_tokens():
     dout = torch.randn(N, D, generator=G).bfloat16().to(DEV)
     bias = zipf_expert_bias(E).to(DEV)
     out, dx, logits = run_layer(layer, x, dout, bias=bias)
+    w_all, idx_all = route_oracle(logits.float().cpu(), k)
     toks = torch.randint(0, N, (16,), generator=G)
-    w, idx = route_oracle(logits.float().cpu()[toks], k)
-    for i, t in enumerate(toks.tolist()):
-        xt = x[t].double()
-        ref = torch.zeros(D, dtype=torch.float64, device=DEV)
-        for j in range(k):
-            e = idx[i, j].item()
-            h = layer.w13[e].double() @ xt
-            a = F.silu(h[:H]) * h[H:]
-            ref += w[i, j].item() * (layer.w2[e].double() @ a)
+    for t in toks.tolist():
+        ref, rdx = _token_reference(layer, x[t].double(), dout[t].double(), w_all[t], idx_all[t], H)
         close(out[t], ref)
-    assert torch.isfinite(dx).all()
+        close(dx[t], rdx)
+    g13, g2 = stacked_grads(layer)
+    load = torch.bincount(idx_all.reshape(-1), minlength=E)
+    order = torch.argsort(load, descending=True, stable=True).tolist()
+    hot = order[0]
+    cold = [e for e in order[::-1] if load[e] > 0][:2]
+    assert load[hot] > 20000, f"hottest expert has only {int(load[hot])} tokens"
+    for e in [hot] + cold:
+        sel = (idx_all == e)
+        tok = sel.any(dim=1).nonzero()[:, 0]
+        we = (w_all * sel).sum(dim=1)[tok].to(DEV)
+        tok = tok.to(DEV)
+        xe = x[tok].float()
+        h = xe @ layer.w13[e].float().t()
+        hb = h.bfloat16().float()  # the kernels keep h1 in bf16
+        g, u = hb[:, :H], hb[:, H:]
+        a = (F.silu(g) * u).bfloat16().float()
+        dy = (dout[tok].float() * we[:, None]).bfloat16().float()
+        close(g2[e], dy.t() @ a)
+        dact = dy @ layer.w2[e].float()
+        s = torch.sigmoid(g)
+        dh1 = torch.cat([dact * u * s * (1 + g * (1 - s)), dact * g * s], dim=1).bfloat16().float()
+        close(g13[e], dh1.t() @ xe)
+
+
+def test_masked_dispatch_layer_api():
+    """tests/test_moe_correctness.py:50-65: FusedMoEMLP(dim=256, hidden_dim=512,
+    n_experts=8, k=2, router_version="v1") on x [2, 64, 256]: output shape, input and
+    router gradients present, and values against the oracle (2e-2 of max magnitude)."""
+    from fusedkernels_b200.moe_layer import FusedMoEMLP
+    torch.manual_seed(2)
+    B, T, D, H = 2, 64, 256, 512
+    moe = FusedMoEMLP(dim=D, hidden_dim=H, n_experts=8, k=2, router_version="v1").to(DEV).bfloat16()
+    x = torch.randn(B, T, D, generator=gen(5)).bfloat16().to(DEV)
+    dout = torch.randn(B, T, D, generator=gen(6)).bfloat16().to(DEV)
+    out, dx, logits = run_layer(moe, x, dout)
+    assert out.shape == x.shape and dx.shape == x.shape
+    assert moe.router.weight.grad is not None
+    w13 = moe.w13.float().cpu()
+    ro, rdx, _, _, _, rdl = moe_layer_oracle(x.reshape(-1, D).cpu(), logits.cpu(), w13[:, :H],
+                                             w13[:, H:], moe.w2.float().cpu(), 2,
+                                             dout.reshape(-1, D).cpu())
+    close(out.reshape(-1, D).cpu(), ro)
+    close(dx.reshape(-1, D).cpu(), rdx + rdl @ moe.router.weight.double().cpu())

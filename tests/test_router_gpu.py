@@ -30,9 +30,16 @@ def check(logits, k, with_bwd=True, seed=0):
     bad = (idx != ridx).any(dim=1).nonzero()
     assert bad.numel() == 0, f"{bad.numel()} rows differ, first {bad[:3].tolist()}"
     torch.testing.assert_close(w, rw, atol=1e-6, rtol=1e-5, equal_nan=True)
-    if with_bwd and logits.dtype == torch.float32:
+    if with_bwd:
         rdl = route_bwd_oracle(logits, k, dw)
-        torch.testing.assert_close(dl, rdl, atol=1e-5, rtol=1e-4)
+        if logits.dtype == torch.float32:
+            torch.testing.assert_close(dl, rdl, atol=1e-5, rtol=1e-4)
+        else:
+            # 16-bit logits: the kernel's fp32 dlogits are cast to the logits dtype by
+            # autograd, so compare with the oracle rounded the same way (one ulp apart at most)
+            ref = rdl.to(logits.dtype).float()
+            torch.testing.assert_close(dl, ref, atol=1e-5, rtol=2 ** -7)
+            assert torch.equal(dl != 0, ref != 0) or (dl - ref).abs().max() < 1e-5
     return w, idx
 
 
@@ -49,10 +56,20 @@ def test_router_fp32_matches_oracle(E, k):
 @pytest.mark.parametrize("E,k", [(8, 2), (64, 8), (128, 8), (128, 16)])
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 def test_router_16bit_ties_bit_exact(E, k, dtype):
-    """16-bit logits tie often; the lower expert index must win every tie."""
+    """16-bit logits tie often; the lower expert index must win every tie.  The backward
+    (the path the MoE layer takes with its bf16 router logits) is checked too."""
     logits = torch.randn(4096, E, generator=gen(11)).to(dtype)
-    w, idx = check(logits, k, with_bwd=False)
+    w, idx = check(logits, k)
     assert idx.shape == (4096, k)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_router_16bit_layer_shape_backward(dtype):
+    """The MoE layer's routing shape: [32768, 128] 16-bit logits, k = 8, with the Zipf
+    expert bias of the workload (skewed, many cross-boundary ties in bf16)."""
+    from oracle import zipf_expert_bias
+    logits = (torch.randn(32768, 128, generator=gen(21)) * 0.3 + zipf_expert_bias(128)).to(dtype)
+    check(logits, 8, seed=21)
 
 
 @pytest.mark.parametrize("n", [1, 3, 1001])
