@@ -45,6 +45,17 @@ SIGNATURES: dict[str, list] = {
     "fk_moe_gemm_down_dgrad": [_vp, _i64, _i32, _vp, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp],
     "fk_moe_gemm_up_dgrad": [_vp, _i64, _i32, _vp, _i32, _i32, _vp, _vp, _vp, _vp, _vp],
     "fk_moe_gemm_wgrad": [_vp, _i32, _vp, _i32, _i64, _vp, _i32, _vp, _vp, _vp],
+    "fk_tf32_split": [_vp, _i64, _vp, _vp, _vp],
+    "fk_moe_gemm_up_typed": [_vp, _vp, _i64, _i32, _vp, _vp, _i32, _i32, _vp, _vp, _vp, _vp,
+                             _i32, _vp, _vp],
+    "fk_moe_gemm_down_typed": [_vp, _vp, _i64, _i32, _vp, _vp, _i32, _i32, _vp, _vp, _vp, _i32,
+                               _vp, _vp],
+    "fk_moe_gemm_down_dgrad_typed": [_vp, _vp, _i64, _i32, _vp, _vp, _i32, _i32, _vp, _vp, _vp,
+                                     _vp, _i32, _vp, _vp],
+    "fk_moe_gemm_up_dgrad_typed": [_vp, _vp, _i64, _i32, _vp, _vp, _i32, _i32, _vp, _vp, _vp,
+                                   _i32, _vp, _vp],
+    "fk_moe_gemm_wgrad_typed": [_vp, _vp, _i32, _vp, _vp, _i32, _i64, _vp, _i32, _vp, _i32, _vp,
+                                _vp],
     "fk_moe_route_meta_skip": [_vp, _vp, _i64, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
                                _i64, _vp, _sz, _vp, _vp],
     "fk_ep_plan_workspace_size": [_i64, _i32, C.POINTER(_sz)],

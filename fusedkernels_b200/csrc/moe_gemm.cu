@@ -1,531 +1,11 @@
-// Grouped GEMMs of the MoE expert MLPs on the 5th-generation tensor cores
-// (tcgen05.mma, accumulators in TMEM, operands staged by TMA), reference
-// moe_layer_sorted.py:70-77 (one cuBLAS call per expert per Linear) and moe_layer.py:22-31.
-//
-// One persistent, warp-specialised kernel template serves every GEMM of the layer:
-//   warp 0      TMA producer: fills a ring of STAGES shared-memory stages (A tile
-//               128 x 64, B tile BN x 64, bf16, 128-byte swizzle) and arms the stage's
-//               "full" mbarrier with the expected byte count;
-//   warp 1      TMEM allocator + MMA issuer: one thread issues 4 tcgen05.mma (K=16 each)
-//               per stage into a 128 x BN fp32 accumulator in TMEM and hands the stage
-//               back with tcgen05.commit on its "empty" mbarrier;
-//   warps 2..5  epilogue: tcgen05.ld the accumulator (each warp owns a 32-lane quarter
-//               of TMEM = 32 rows of the tile), apply the fused epilogue, store bf16.
-// Two accumulators (2*BN TMEM columns) let the epilogue of tile i overlap the MMAs of
-// tile i+1.  Tiles are handed out round-robin to one CTA per SM.
-//
-// Grouping.  MODE_M: rows of A are the expert-sorted assignment rows; every 128-row
-// block belongs to one expert (segments are padded to 128 rows), whose weight matrix is
-// the B operand (3-D tensor map over [E, rows, cols]).  The number of valid row blocks
-// is read on the device, so no host synchronisation is needed.  MODE_K (weight
-// gradients): for expert e the reduction runs over its token segment; A and B are
-// token-major (MN-major operands) and the output is expert e's [M, N] gradient.
-//
-// Epilogue stores go through a per-warp ring of shared-memory chunks and TMA stores
-// (coalesced 64-byte rows instead of per-thread 16-byte row fragments).
-// Epilogues: plain bf16 store; SwiGLU forward (the B tile holds BN/2 gate rows and the
-// matching BN/2 up rows, so the tile yields h1 = (g, u) and act = silu(g) * u); SwiGLU
-// backward (reads g, u of the tile's hidden units and writes (dg, du)).
-//
-// No load uses cluster multicast: every CTA fetches its own tiles.  Every mbarrier wait
-// is bounded by a wall-clock budget; a timeout records an error code and the CTA leaves
-// its loops (the accumulator memory is still released).
-#include <cuda.h>
-
-#include "common.cuh"
-#include "ptx.cuh"
+// bf16 entry points of the MoE expert GEMMs (kernel template and per-GEMM set-up in
+// moe_gemm.cuh), reference moe_layer_sorted.py:70-77 and moe_layer.py:22-31.
+#include "moe_gemm.cuh"
 
 namespace fk {
 namespace gemm {
 
-constexpr int BM = 128;
-constexpr int BK = 64;
-constexpr int kThreads = 192;
-constexpr int kMaxGemmExperts = 256;  // expert ids of the weight-gradient schedule fit a byte
-constexpr uint64_t kWaitNs = 2000000000ull;  // 2 s per wait: far above any legitimate wait
-
-enum Mode { MODE_M = 0, MODE_K = 1 };
-enum Epi { EPI_STORE = 0, EPI_SWIGLU_FWD = 1, EPI_SWIGLU_BWD = 2 };
-
-struct Params {
-  int M, N, K;   // MODE_M: N = output columns (SwiGLU fwd: hidden units H), K = reduction
-                 // MODE_K: per-expert output [M, N]
-  int E, H;
-  const int* seg_start;    // [E+1] padded token offsets
-  const int* tile_expert;  // [rows/128] expert of each 128-row block (MODE_M)
-  const int* n_mblk;       // valid 128-row blocks (MODE_M)
-  __nv_bfloat16* out0;     // STORE: C; SWIGLU_FWD: act [rows, H]; SWIGLU_BWD: dh1 [rows, 2H]
-  int64_t ld0;
-  __nv_bfloat16* out1;     // SWIGLU_FWD: h1 [rows, 2H]
-  int64_t ld1;
-  const __nv_bfloat16* in0;  // SWIGLU_BWD: h1 [rows, 2H]
-  int64_t ldi0;
-  int* err;
-  int tma_store;  // epilogue writes through shared memory + TMA stores (tmC0 / tmC1)
-};
-
-__device__ __forceinline__ uint64_t globaltimer() {
-  uint64_t t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}
-
-// Bounded mbarrier wait (wall clock); records `code` in *err on timeout.
-__device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, int* err, int code) {
-  if (ptx::mbar_try_wait(bar, parity)) return true;
-  const uint64_t t0 = globaltimer();
-  for (uint32_t i = 1;; ++i) {
-    if (ptx::mbar_try_wait(bar, parity)) return true;
-    if ((i & 255u) == 0 && globaltimer() - t0 > kWaitNs) {
-      atomicExch(err, code);
-      return false;
-    }
-  }
-}
-
-__device__ __forceinline__ void tma2d(void* dst, const CUtensorMap* map, int c0, int c1,
-                                      uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%2, %3}], [%4];" ::"r"(ptx::smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(ptx::smem_u32(bar))
-      : "memory");
-}
-__device__ __forceinline__ void tma3d(void* dst, const CUtensorMap* map, int c0, int c1, int c2,
-                                      uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(ptx::smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(ptx::smem_u32(bar))
-      : "memory");
-}
-
-// Shared-memory matrix descriptor, 128-byte swizzle, sm_100 version bit.
-__device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
-  uint64_t d = 0;
-  d |= (uint64_t)((addr & 0x3FFFFu) >> 4);
-  d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
-  d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;
-  d |= (uint64_t)1 << 46;  // descriptor version (sm_100)
-  d |= (uint64_t)2 << 61;  // SWIZZLE_128B
-  return d;
-}
-
-__device__ __forceinline__ void mma_bf16(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc,
-                                         uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "l"(a), "l"(b), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-__device__ __forceinline__ void mma_commit(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::
-                   "r"(ptx::smem_u32(bar))
-               : "memory");
-}
-__device__ __forceinline__ void tc_fence_before() {
-  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-}
-__device__ __forceinline__ void tc_fence_after() {
-  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-}
-
-// 32 lanes x 32 consecutive fp32 columns: thread i of the warp gets row (lane base + i).
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
-  uint32_t r[32];
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
-      "%11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, "
-      "%28, %29, %30, %31}, [%32];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
-        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
-        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
-        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
-        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
-}
-
-__device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
-  __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
-  return *reinterpret_cast<uint32_t*>(&h);
-}
-
-// Store 32 fp32 values as bf16 at dst (64 contiguous bytes, 16-byte aligned).
-__device__ __forceinline__ void store32(__nv_bfloat16* dst, const float (&v)[32]) {
-  uint4* d = reinterpret_cast<uint4*>(dst);
-#pragma unroll
-  for (int q = 0; q < 4; ++q)
-    d[q] = make_uint4(pack_bf16(v[8 * q], v[8 * q + 1]), pack_bf16(v[8 * q + 2], v[8 * q + 3]),
-                      pack_bf16(v[8 * q + 4], v[8 * q + 5]), pack_bf16(v[8 * q + 6], v[8 * q + 7]));
-}
-
-__device__ __forceinline__ void load32(const __nv_bfloat16* src, float (&v)[32]) {
-  const uint4* s = reinterpret_cast<const uint4*>(src);
-#pragma unroll
-  for (int q = 0; q < 4; ++q) {
-    uint4 u = s[q];
-    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      float2 f = __bfloat1622float2(h[j]);
-      v[8 * q + 2 * j] = f.x;
-      v[8 * q + 2 * j + 1] = f.y;
-    }
-  }
-}
-
-// Epilogue output path: each epilogue warp owns a ring of kRingBufs 2 KB shared-memory
-// buffers; a 32-row x 32-column bf16 chunk is written into one (64-byte rows, 64-byte
-// swizzle, so the 16-byte writes of a warp hit distinct banks) and stored to global memory
-// by one TMA store issued by lane 0.  A buffer is reused only after the bulk store that
-// read it four chunks earlier has finished reading.
-constexpr int kRingBufs = 4;
-constexpr uint32_t kChunkBytes = 32 * 32 * 2;
-constexpr uint32_t kRingBytesPerWarp = kRingBufs * kChunkBytes;
-
-struct StoreRing {
-  uint32_t base;
-  int next;
-  __device__ __forceinline__ void put(const CUtensorMap* map, int col, int row,
-                                      const float (&v)[32], int lane) {
-    if (lane == 0) asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(kRingBufs - 1) : "memory");
-    __syncwarp();
-    const uint32_t buf = base + (uint32_t)next * kChunkBytes;
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const uint32_t addr = buf + (uint32_t)lane * 64u + ((uint32_t)(q ^ ((lane >> 1) & 3)) << 4);
-      asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr),
-                   "r"(pack_bf16(v[8 * q], v[8 * q + 1])), "r"(pack_bf16(v[8 * q + 2], v[8 * q + 3])),
-                   "r"(pack_bf16(v[8 * q + 4], v[8 * q + 5])), "r"(pack_bf16(v[8 * q + 6], v[8 * q + 7]))
-                   : "memory");
-    }
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-    __syncwarp();
-    if (lane == 0) {
-      asm volatile(
-          "cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
-              reinterpret_cast<uint64_t>(map)),
-          "r"(col), "r"(row), "r"(buf)
-          : "memory");
-      asm volatile("cp.async.bulk.commit_group;" ::: "memory");
-    }
-    next = (next + 1) & (kRingBufs - 1);
-  }
-  __device__ __forceinline__ void drain(int lane) {
-    if (lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
-    __syncwarp();
-  }
-};
-
-struct Tile {
-  int e, m0, n0, kb0, kiters;
-  bool valid;
-};
-
-template <int BN, int MODE, int EPI>
-__device__ __forceinline__ int num_tiles(const Params& p) {
-  if (MODE == MODE_M) {
-    const int nnb = (EPI == EPI_SWIGLU_FWD) ? p.H / (BN / 2) : p.N / BN;
-    return (*p.n_mblk) * nnb;
-  }
-  const int nmb = (p.M + BM - 1) / BM, nnb = p.N / BN;
-  return p.E * nmb * nnb;
-}
-
-// MODE_K visits the experts in descending order of their token count (order[]) and hands
-// the tiles out in a serpentine over the CTAs (pass i goes left to right when i is even,
-// right to left when odd), so the tiles of the few hot experts of a skewed routing spread
-// evenly over the SMs instead of piling up on the CTAs their position happens to hit.
-// t runs over whole passes; tiles past the end are invalid.
-template <int BN, int MODE, int EPI>
-__device__ __forceinline__ Tile decode(const Params& p, int t, const uint8_t* order, int ntiles) {
-  Tile tl;
-  tl.valid = true;
-  if (MODE == MODE_M) {
-    const int nnb = (EPI == EPI_SWIGLU_FWD) ? p.H / (BN / 2) : p.N / BN;
-    const int mb = t / nnb, nb = t % nnb;
-    tl.e = p.tile_expert[mb];
-    tl.valid = tl.e >= 0;
-    tl.m0 = mb * BM;
-    tl.n0 = nb * ((EPI == EPI_SWIGLU_FWD) ? BN / 2 : BN);
-    tl.kb0 = 0;
-    tl.kiters = p.K / BK;
-  } else {
-    const int nmb = (p.M + BM - 1) / BM, nnb = p.N / BN;
-    const int G = gridDim.x, pass = t / G, j = t % G;
-    const int g = pass * G + ((pass & 1) ? G - 1 - j : j);
-    if (g >= ntiles) {
-      tl.valid = false;
-      return tl;
-    }
-    tl.e = order[g / (nmb * nnb)];
-    const int r = g % (nmb * nnb);
-    tl.m0 = (r / nnb) * BM;
-    tl.n0 = (r % nnb) * BN;
-    const int s0 = p.seg_start[tl.e], s1 = p.seg_start[tl.e + 1];
-    tl.kb0 = s0 / BK;
-    tl.kiters = (s1 - s0) / BK;
-  }
-  return tl;
-}
-
-template <int BN, int STAGES, bool A_MN, bool B_MN, int MODE, int EPI>
-__global__ void __launch_bounds__(kThreads, 1)
-    moe_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
-                    const __grid_constant__ CUtensorMap tmB,
-                    const __grid_constant__ CUtensorMap tmC0,
-                    const __grid_constant__ CUtensorMap tmC1, const Params p) {
-  constexpr uint32_t A_BYTES = BM * BK * 2;
-  constexpr uint32_t B_BYTES = BN * BK * 2;
-  constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
-  constexpr uint32_t TMEM_COLS = 2 * BN;
-  extern __shared__ __align__(1024) unsigned char smem_raw[];
-  unsigned char* smem = reinterpret_cast<unsigned char*>(
-      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  const uint32_t ring_base = ptx::smem_u32(smem + STAGES * STAGE_BYTES);  // 4 warps x ring
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES + 4 * kRingBytesPerWarp);
-  uint64_t* empty = full + STAGES;
-  uint64_t* tfull = empty + STAGES;
-  uint64_t* tempty = tfull + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
-
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  __shared__ uint8_t order[kMaxGemmExperts];  // MODE_K: experts by descending token count
-  if (MODE == MODE_K) {
-    for (int e = threadIdx.x; e < p.E; e += blockDim.x) {
-      const int len = p.seg_start[e + 1] - p.seg_start[e];
-      int rank = 0;
-      for (int f = 0; f < p.E; ++f) {
-        const int lf = p.seg_start[f + 1] - p.seg_start[f];
-        rank += (lf > len) || (lf == len && f < e);
-      }
-      order[rank] = (uint8_t)e;
-    }
-  }
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < STAGES; ++s) {
-      ptx::mbar_init(&full[s], 1);
-      ptx::mbar_init(&empty[s], 1);
-    }
-    for (int a = 0; a < 2; ++a) {
-      ptx::mbar_init(&tfull[a], 1);
-      ptx::mbar_init(&tempty[a], 128);
-    }
-    ptx::fence_mbar_init();
-  }
-  if (warp == 1) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
-                     ptx::smem_u32(tmem_slot)),
-                 "r"(TMEM_COLS)
-                 : "memory");
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem_base = *tmem_slot;
-  const int ntiles = num_tiles<BN, MODE, EPI>(p);
-  const int tiles_loop =
-      MODE == MODE_K ? (ntiles + (int)gridDim.x - 1) / (int)gridDim.x * (int)gridDim.x : ntiles;
-
-  if (warp == 0) {
-    if (lane == 0) {
-      // ------------------------------------------------------------ TMA producer
-      int s = 0;
-      uint32_t ph = 0;
-      bool ok = true;
-      for (int t = blockIdx.x; t < tiles_loop && ok; t += gridDim.x) {
-        const Tile tl = decode<BN, MODE, EPI>(p, t, order, ntiles);
-        if (!tl.valid) continue;
-        for (int kb = 0; kb < tl.kiters; ++kb) {
-          if (!wait_bar(&empty[s], ph ^ 1, p.err, 11)) { ok = false; break; }
-          unsigned char* sa = smem + s * STAGE_BYTES;
-          unsigned char* sb = sa + A_BYTES;
-          ptx::mbar_arrive_expect_tx(&full[s], STAGE_BYTES);
-          const int k0 = (tl.kb0 + kb) * BK;
-          if (!A_MN) {
-            tma2d(sa, &tmA, k0, tl.m0, &full[s]);
-          } else {
-            tma2d(sa, &tmA, tl.m0, k0, &full[s]);
-            tma2d(sa + 8192, &tmA, tl.m0 + 64, k0, &full[s]);
-          }
-          if (EPI == EPI_SWIGLU_FWD) {
-            tma3d(sb, &tmB, k0, tl.n0, tl.e, &full[s]);
-            tma3d(sb + (BN / 2) * 128, &tmB, k0, p.H + tl.n0, tl.e, &full[s]);
-          } else if (!B_MN) {
-            tma3d(sb, &tmB, k0, tl.n0, tl.e, &full[s]);
-          } else if (MODE == MODE_M) {
-#pragma unroll
-            for (int i = 0; i < BN / 64; ++i) tma3d(sb + i * 8192, &tmB, tl.n0 + 64 * i, k0, tl.e, &full[s]);
-          } else {
-#pragma unroll
-            for (int i = 0; i < BN / 64; ++i) tma2d(sb + i * 8192, &tmB, tl.n0 + 64 * i, k0, &full[s]);
-          }
-          if (++s == STAGES) { s = 0; ph ^= 1; }
-        }
-      }
-    }
-  } else if (warp == 1) {
-    if (lane == 0) {
-      // ------------------------------------------------------------ MMA issuer
-      constexpr uint32_t idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((A_MN ? 1u : 0u) << 15) |
-                                 ((B_MN ? 1u : 0u) << 16) | ((uint32_t)(BN >> 3) << 17) |
-                                 ((uint32_t)(BM >> 4) << 24);
-      int s = 0;
-      uint32_t ph = 0;
-      int it = 0;
-      bool ok = true;
-      for (int t = blockIdx.x; t < tiles_loop && ok; t += gridDim.x) {
-        const Tile tl = decode<BN, MODE, EPI>(p, t, order, ntiles);
-        if (!tl.valid) continue;
-        const int acc = it & 1;
-        const uint32_t aph = (uint32_t)((it >> 1) & 1);
-        ++it;
-        if (!wait_bar(&tempty[acc], aph ^ 1, p.err, 12)) break;
-        tc_fence_after();
-        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
-        if (tl.kiters == 0) {
-          ptx::mbar_arrive(&tfull[acc]);
-          continue;
-        }
-        for (int kb = 0; kb < tl.kiters; ++kb) {
-          if (!wait_bar(&full[s], ph, p.err, 13)) { ok = false; break; }
-          tc_fence_after();
-          const uint32_t a_base = ptx::smem_u32(smem + s * STAGE_BYTES);
-          const uint32_t b_base = a_base + A_BYTES;
-#pragma unroll
-          for (int ks = 0; ks < BK / 16; ++ks) {
-            const uint64_t ad = A_MN ? smem_desc(a_base + ks * 2048, 8192, 1024)
-                                     : smem_desc(a_base + ks * 32, 16, 1024);
-            const uint64_t bd = B_MN ? smem_desc(b_base + ks * 2048, 8192, 1024)
-                                     : smem_desc(b_base + ks * 32, 16, 1024);
-            mma_bf16(d_tmem, ad, bd, idesc, (kb | ks) != 0);
-          }
-          mma_commit(&empty[s]);
-          if (++s == STAGES) { s = 0; ph ^= 1; }
-        }
-        mma_commit(&tfull[acc]);
-      }
-    }
-  } else {
-    // -------------------------------------------------------------- epilogue (128 thr)
-    const int q = warp & 3;  // TMEM lane quarter this warp may access
-    const int row_in_tile = q * 32 + lane;
-    StoreRing ring{ring_base + (uint32_t)(warp - 2) * kRingBytesPerWarp, 0};
-    int it = 0;
-    for (int t = blockIdx.x; t < tiles_loop; t += gridDim.x) {
-      const Tile tl = decode<BN, MODE, EPI>(p, t, order, ntiles);
-      if (!tl.valid) continue;
-      const int acc = it & 1;
-      const uint32_t aph = (uint32_t)((it >> 1) & 1);
-      ++it;
-      if (!wait_bar(&tfull[acc], aph, p.err, 14)) break;
-      tc_fence_after();
-      const uint32_t tbase = tmem_base + (uint32_t)(acc * BN) + ((uint32_t)(q * 32) << 16);
-      const bool zero = tl.kiters == 0;
-      const int row0 = tl.m0 + q * 32;  // first row of this warp's 32-row slab
-      if (MODE == MODE_K) {
-        // tcgen05.ld is warp-collective: every lane loads, only rows < M store.
-        const int m = tl.m0 + row_in_tile;
-        __nv_bfloat16* dst = p.out0 + ((int64_t)tl.e * p.M + m) * p.ld0 + tl.n0;
-#pragma unroll 1
-        for (int c = 0; c < BN; c += 32) {
-          float v[32];
-          if (zero) {
-#pragma unroll
-            for (int i = 0; i < 32; ++i) v[i] = 0.f;
-          } else {
-            tmem_ld32(tbase + c, v);
-          }
-          if (p.tma_store) ring.put(&tmC0, tl.n0 + c, tl.e * p.M + row0, v, lane);
-          else if (m < p.M) store32(dst + c, v);
-        }
-      } else {
-        const int64_t row = tl.m0 + row_in_tile;
-        if (EPI == EPI_STORE) {
-          __nv_bfloat16* dst = p.out0 + row * p.ld0 + tl.n0;
-#pragma unroll 1
-          for (int c = 0; c < BN; c += 32) {
-            float v[32];
-            tmem_ld32(tbase + c, v);
-            if (p.tma_store) ring.put(&tmC0, tl.n0 + c, row0, v, lane);
-            else store32(dst + c, v);
-          }
-        } else if (EPI == EPI_SWIGLU_FWD) {
-          __nv_bfloat16* act = p.out0 + row * p.ld0 + tl.n0;
-          __nv_bfloat16* hg = p.out1 + row * p.ld1 + tl.n0;
-          __nv_bfloat16* hu = p.out1 + row * p.ld1 + p.H + tl.n0;
-#pragma unroll 1
-          for (int c = 0; c < BN / 2; c += 32) {
-            float g[32], u[32], a[32];
-            tmem_ld32(tbase + c, g);
-            tmem_ld32(tbase + BN / 2 + c, u);
-#pragma unroll
-            for (int i = 0; i < 32; ++i) a[i] = g[i] * sigmoidf_t<__nv_bfloat16>(g[i]) * u[i];
-            if (p.tma_store) {
-              ring.put(&tmC1, tl.n0 + c, row0, g, lane);
-              ring.put(&tmC1, p.H + tl.n0 + c, row0, u, lane);
-              ring.put(&tmC0, tl.n0 + c, row0, a, lane);
-            } else {
-              store32(hg + c, g);
-              store32(hu + c, u);
-              store32(act + c, a);
-            }
-          }
-        } else {  // EPI_SWIGLU_BWD: accumulator = d(act) for hidden units n0 .. n0+BN
-          const __nv_bfloat16* hg = p.in0 + row * p.ldi0 + tl.n0;
-          const __nv_bfloat16* hu = p.in0 + row * p.ldi0 + p.H + tl.n0;
-          __nv_bfloat16* dg = p.out0 + row * p.ld0 + tl.n0;
-          __nv_bfloat16* du = p.out0 + row * p.ld0 + p.H + tl.n0;
-#pragma unroll 1
-          for (int c = 0; c < BN; c += 32) {
-            float d[32], g[32], u[32], og[32], ou[32];
-            tmem_ld32(tbase + c, d);
-            load32(hg + c, g);
-            load32(hu + c, u);
-#pragma unroll
-            for (int i = 0; i < 32; ++i) {
-              const float sg = sigmoidf_t<__nv_bfloat16>(g[i]);
-              ou[i] = d[i] * g[i] * sg;
-              og[i] = d[i] * u[i] * (sg * (1.0f + g[i] * (1.0f - sg)));
-            }
-            if (p.tma_store) {
-              ring.put(&tmC0, tl.n0 + c, row0, og, lane);
-              ring.put(&tmC0, p.H + tl.n0 + c, row0, ou, lane);
-            } else {
-              store32(dg + c, og);
-              store32(du + c, ou);
-            }
-          }
-        }
-      }
-      tc_fence_before();
-      ptx::mbar_arrive(&tempty[acc]);
-    }
-    ring.drain(lane);
-  }
-  tc_fence_before();
-  __syncthreads();
-  if (warp == 1) {
-    tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
-                 "r"(TMEM_COLS)
-                 : "memory");
-  }
-}
-
-// ------------------------------------------------------------------ host side -----------
-typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
-                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
-                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
-                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-static EncodeTiledFn encode_fn() {
+EncodeTiledFn encode_fn() {
   // looked up once (thread-safe static initialisation)
   static const EncodeTiledFn fn = [] {
     void* f = nullptr;
@@ -538,270 +18,45 @@ static EncodeTiledFn encode_fn() {
   return fn;
 }
 
-// bf16 tensor map, 128-byte swizzle; dims/strides innermost first (strides in bytes,
-// rank-1 entries), box innermost first.
-static int make_map(CUtensorMap* m, const void* base, int rank, const uint64_t* dims,
-                    const uint64_t* strides, const uint32_t* box,
-                    CUtensorMapSwizzle swz = CU_TENSOR_MAP_SWIZZLE_128B) {
-  EncodeTiledFn fn = encode_fn();
-  if (!fn) return fail(FK_ERR_NO_DEVICE, "cuTensorMapEncodeTiled unavailable");
-  cuuint64_t d[3], st[2];
-  cuuint32_t b[3], es[3] = {1, 1, 1};
-  for (int i = 0; i < rank; ++i) {
-    d[i] = dims[i];
-    b[i] = box[i];
-  }
-  for (int i = 0; i < rank - 1; ++i) st[i] = strides[i];
-  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, rank, const_cast<void*>(base), d, st, b, es,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
-                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) return fail(FK_ERR_INVALID_ARG, "cuTensorMapEncodeTiled failed (%d)", (int)r);
-  return FK_OK;
-}
-
-// Epilogue output map: bf16 [rows, cols] (row stride ld elements), 32 x 32 boxes, 64-byte
-// swizzle (matching the StoreRing layout).
-static int make_out_map(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, int64_t ld) {
-  uint64_t d[2] = {(uint64_t)cols, (uint64_t)rows}, st[1] = {(uint64_t)ld * 2};
-  uint32_t box[2] = {32, 32};
-  return make_map(m, base, 2, d, st, box, CU_TENSOR_MAP_SWIZZLE_64B);
-}
-
-template <int BN, bool A_MN, bool B_MN, int MODE, int EPI>
-static int launch(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& c0,
-                  const CUtensorMap& c1, const Params& p, int max_tiles, cudaStream_t st) {
-  constexpr int STAGE_BYTES = (BM + BN) * BK * 2;
-  constexpr int STAGES = (BN == 256) ? 4 : (BN == 128 ? 6 : 8);
-  constexpr int SMEM = STAGES * STAGE_BYTES + 4 * (int)kRingBytesPerWarp + 1024 + 256;
-  auto k = moe_gemm_kernel<BN, STAGES, A_MN, B_MN, MODE, EPI>;
-  cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
-  int grid = num_sms();
-  if (max_tiles < grid) grid = max_tiles < 1 ? 1 : max_tiles;
-  k<<<grid, kThreads, SMEM, st>>>(a, b, c0, c1, p);
-  return launch_status("fk_moe_gemm");
-}
-
-static int pick_bn(int n) {
-  if (n % 256 == 0) return 256;
-  if (n % 128 == 0) return 128;
-  if (n % 64 == 0) return 64;
-  return 0;
-}
-
 }  // namespace gemm
 }  // namespace fk
 
-using fk::gemm::Params;
 namespace G = fk::gemm;
-
-#define FK_BN_SWITCH(bn, ...)                                 \
-  switch (bn) {                                               \
-    case 256: { constexpr int BN_ = 256; __VA_ARGS__; break; } \
-    case 128: { constexpr int BN_ = 128; __VA_ARGS__; break; } \
-    case 64: { constexpr int BN_ = 64; __VA_ARGS__; break; }   \
-    default: return fk::fail(FK_ERR_UNSUPPORTED, "unsupported tile width"); \
-  }
-
-static int check_common(const void* a, const void* b, const int* tile_expert, const int* n_mblk,
-                        int64_t max_rows, int E) {
-  FK_CHECK_ARG(a && b && tile_expert && n_mblk, "fk_moe_gemm: null pointer");
-  FK_CHECK_ARG(max_rows >= 0 && max_rows % G::BM == 0, "fk_moe_gemm: max_rows must be a multiple of 128");
-  FK_CHECK_ARG(E >= 1, "fk_moe_gemm: E < 1");
-  FK_CHECK_ARG(fk::aligned16(a) && fk::aligned16(b), "fk_moe_gemm: operands must be 16-byte aligned");
-  return FK_OK;
-}
 
 extern "C" int fk_moe_gemm_up(const void* xs, int64_t max_rows, int dim, const void* w13,
                               int hidden, int n_experts, const int* tile_expert, const int* n_mblk,
                               void* h1, void* act, int* err_flag, void* stream) {
-  int st = check_common(xs, w13, tile_expert, n_mblk, max_rows, n_experts);
-  if (st) return st;
-  FK_CHECK_ARG(h1 && act && err_flag, "fk_moe_gemm_up: null pointer");
-  FK_CHECK_ARG(dim % 64 == 0 && hidden % 64 == 0, "fk_moe_gemm_up: dim, hidden must be multiples of 64");
-  if (max_rows == 0) return FK_OK;
-  const int bn = (hidden % 128 == 0) ? 256 : 128;
-  CUtensorMap ma, mb;
-  uint64_t da[2] = {(uint64_t)dim, (uint64_t)max_rows}, sa[1] = {(uint64_t)dim * 2};
-  uint32_t ba[2] = {64, 128};
-  if ((st = G::make_map(&ma, xs, 2, da, sa, ba))) return st;
-  uint64_t db[3] = {(uint64_t)dim, (uint64_t)2 * hidden, (uint64_t)n_experts};
-  uint64_t sb[2] = {(uint64_t)dim * 2, (uint64_t)2 * hidden * dim * 2};
-  uint32_t bb[3] = {64, (uint32_t)bn / 2, 1};
-  if ((st = G::make_map(&mb, w13, 3, db, sb, bb))) return st;
-  Params p{};
-  p.M = (int)max_rows;
-  p.N = hidden;
-  p.K = dim;
-  p.E = n_experts;
-  p.H = hidden;
-  p.tile_expert = tile_expert;
-  p.n_mblk = n_mblk;
-  p.out0 = static_cast<__nv_bfloat16*>(act);
-  p.ld0 = hidden;
-  p.out1 = static_cast<__nv_bfloat16*>(h1);
-  p.ld1 = 2 * (int64_t)hidden;
-  p.err = err_flag;
-  const int max_tiles = (int)(max_rows / G::BM) * (hidden / (bn / 2));
-  CUtensorMap mc0, mc1;
-  if ((st = G::make_out_map(&mc0, act, max_rows, hidden, hidden))) return st;
-  if ((st = G::make_out_map(&mc1, h1, max_rows, 2 * hidden, 2 * hidden))) return st;
-  p.tma_store = 1;
-  cudaStream_t s = fk::as_stream(stream);
-  if (bn == 256)
-    return G::launch<256, false, false, G::MODE_M, G::EPI_SWIGLU_FWD>(ma, mb, mc0, mc1, p, max_tiles, s);
-  return G::launch<128, false, false, G::MODE_M, G::EPI_SWIGLU_FWD>(ma, mb, mc0, mc1, p, max_tiles, s);
+  return G::gemm_up<G::KIND_BF16>(xs, nullptr, max_rows, dim, w13, nullptr, hidden, n_experts,
+                                  tile_expert, n_mblk, h1, act, err_flag, fk::as_stream(stream));
 }
 
 extern "C" int fk_moe_gemm_down(const void* act, int64_t max_rows, int hidden, const void* w2,
                                 int dim, int n_experts, const int* tile_expert, const int* n_mblk,
                                 void* y, int* err_flag, void* stream) {
-  int st = check_common(act, w2, tile_expert, n_mblk, max_rows, n_experts);
-  if (st) return st;
-  FK_CHECK_ARG(y && err_flag, "fk_moe_gemm_down: null pointer");
-  FK_CHECK_ARG(hidden % 64 == 0 && dim % 64 == 0, "fk_moe_gemm_down: dim, hidden must be multiples of 64");
-  if (max_rows == 0) return FK_OK;
-  const int bn = G::pick_bn(dim);
-  CUtensorMap ma, mb;
-  uint64_t da[2] = {(uint64_t)hidden, (uint64_t)max_rows}, sa[1] = {(uint64_t)hidden * 2};
-  uint32_t ba[2] = {64, 128};
-  if ((st = G::make_map(&ma, act, 2, da, sa, ba))) return st;
-  uint64_t db[3] = {(uint64_t)hidden, (uint64_t)dim, (uint64_t)n_experts};
-  uint64_t sb[2] = {(uint64_t)hidden * 2, (uint64_t)dim * hidden * 2};
-  uint32_t bb[3] = {64, (uint32_t)bn, 1};
-  if ((st = G::make_map(&mb, w2, 3, db, sb, bb))) return st;
-  Params p{};
-  p.M = (int)max_rows;
-  p.N = dim;
-  p.K = hidden;
-  p.E = n_experts;
-  p.H = hidden;
-  p.tile_expert = tile_expert;
-  p.n_mblk = n_mblk;
-  p.out0 = static_cast<__nv_bfloat16*>(y);
-  p.ld0 = dim;
-  p.err = err_flag;
-  const int max_tiles = (int)(max_rows / G::BM) * (dim / bn);
-  CUtensorMap mc0;
-  if ((st = G::make_out_map(&mc0, y, max_rows, dim, dim))) return st;
-  p.tma_store = 1;
-  cudaStream_t s = fk::as_stream(stream);
-  FK_BN_SWITCH(bn, return G::launch<BN_, false, false, G::MODE_M, G::EPI_STORE>(ma, mb, mc0, mc0, p, max_tiles, s));
-  return FK_OK;
+  return G::gemm_down<G::KIND_BF16>(act, nullptr, max_rows, hidden, w2, nullptr, dim, n_experts,
+                                    tile_expert, n_mblk, y, err_flag, fk::as_stream(stream));
 }
 
 extern "C" int fk_moe_gemm_down_dgrad(const void* dy, int64_t max_rows, int dim, const void* w2,
                                       int hidden, int n_experts, const int* tile_expert,
                                       const int* n_mblk, const void* h1, void* dh1, int* err_flag,
                                       void* stream) {
-  int st = check_common(dy, w2, tile_expert, n_mblk, max_rows, n_experts);
-  if (st) return st;
-  FK_CHECK_ARG(h1 && dh1 && err_flag, "fk_moe_gemm_down_dgrad: null pointer");
-  FK_CHECK_ARG(hidden % 64 == 0 && dim % 64 == 0, "fk_moe_gemm_down_dgrad: dim, hidden must be multiples of 64");
-  if (max_rows == 0) return FK_OK;
-  const int bn = G::pick_bn(hidden);
-  CUtensorMap ma, mb;
-  uint64_t da[2] = {(uint64_t)dim, (uint64_t)max_rows}, sa[1] = {(uint64_t)dim * 2};
-  uint32_t ba[2] = {64, 128};
-  if ((st = G::make_map(&ma, dy, 2, da, sa, ba))) return st;
-  // B[n = h, k = d] = W2[e][d][h]: hidden-contiguous (MN-major) boxes of 64 x 64.
-  uint64_t db[3] = {(uint64_t)hidden, (uint64_t)dim, (uint64_t)n_experts};
-  uint64_t sb[2] = {(uint64_t)hidden * 2, (uint64_t)dim * hidden * 2};
-  uint32_t bb[3] = {64, 64, 1};
-  if ((st = G::make_map(&mb, w2, 3, db, sb, bb))) return st;
-  Params p{};
-  p.M = (int)max_rows;
-  p.N = hidden;
-  p.K = dim;
-  p.E = n_experts;
-  p.H = hidden;
-  p.tile_expert = tile_expert;
-  p.n_mblk = n_mblk;
-  p.out0 = static_cast<__nv_bfloat16*>(dh1);
-  p.ld0 = 2 * (int64_t)hidden;
-  p.in0 = static_cast<const __nv_bfloat16*>(h1);
-  p.ldi0 = 2 * (int64_t)hidden;
-  p.err = err_flag;
-  const int max_tiles = (int)(max_rows / G::BM) * (hidden / bn);
-  CUtensorMap mc0;
-  if ((st = G::make_out_map(&mc0, dh1, max_rows, 2 * hidden, 2 * hidden))) return st;
-  p.tma_store = 1;
-  cudaStream_t s = fk::as_stream(stream);
-  FK_BN_SWITCH(bn, return G::launch<BN_, false, true, G::MODE_M, G::EPI_SWIGLU_BWD>(ma, mb, mc0, mc0, p, max_tiles, s));
-  return FK_OK;
+  return G::gemm_down_dgrad<G::KIND_BF16>(dy, nullptr, max_rows, dim, w2, nullptr, hidden,
+                                          n_experts, tile_expert, n_mblk, h1, dh1, err_flag,
+                                          fk::as_stream(stream));
 }
 
 extern "C" int fk_moe_gemm_up_dgrad(const void* dh1, int64_t max_rows, int hidden, const void* w13,
                                     int dim, int n_experts, const int* tile_expert,
                                     const int* n_mblk, void* dxs, int* err_flag, void* stream) {
-  int st = check_common(dh1, w13, tile_expert, n_mblk, max_rows, n_experts);
-  if (st) return st;
-  FK_CHECK_ARG(dxs && err_flag, "fk_moe_gemm_up_dgrad: null pointer");
-  FK_CHECK_ARG(hidden % 64 == 0 && dim % 64 == 0, "fk_moe_gemm_up_dgrad: dim, hidden must be multiples of 64");
-  if (max_rows == 0) return FK_OK;
-  const int bn = G::pick_bn(dim);
-  CUtensorMap ma, mb;
-  uint64_t da[2] = {(uint64_t)2 * hidden, (uint64_t)max_rows}, sa[1] = {(uint64_t)2 * hidden * 2};
-  uint32_t ba[2] = {64, 128};
-  if ((st = G::make_map(&ma, dh1, 2, da, sa, ba))) return st;
-  // B[n = d, k = j] = W13[e][j][d]: dim-contiguous (MN-major) boxes of 64 x 64.
-  uint64_t db[3] = {(uint64_t)dim, (uint64_t)2 * hidden, (uint64_t)n_experts};
-  uint64_t sb[2] = {(uint64_t)dim * 2, (uint64_t)2 * hidden * dim * 2};
-  uint32_t bb[3] = {64, 64, 1};
-  if ((st = G::make_map(&mb, w13, 3, db, sb, bb))) return st;
-  Params p{};
-  p.M = (int)max_rows;
-  p.N = dim;
-  p.K = 2 * hidden;
-  p.E = n_experts;
-  p.H = hidden;
-  p.tile_expert = tile_expert;
-  p.n_mblk = n_mblk;
-  p.out0 = static_cast<__nv_bfloat16*>(dxs);
-  p.ld0 = dim;
-  p.err = err_flag;
-  const int max_tiles = (int)(max_rows / G::BM) * (dim / bn);
-  CUtensorMap mc0;
-  if ((st = G::make_out_map(&mc0, dxs, max_rows, dim, dim))) return st;
-  p.tma_store = 1;
-  cudaStream_t s = fk::as_stream(stream);
-  FK_BN_SWITCH(bn, return G::launch<BN_, false, true, G::MODE_M, G::EPI_STORE>(ma, mb, mc0, mc0, p, max_tiles, s));
-  return FK_OK;
+  return G::gemm_up_dgrad<G::KIND_BF16>(dh1, nullptr, max_rows, hidden, w13, nullptr, dim,
+                                        n_experts, tile_expert, n_mblk, dxs, err_flag,
+                                        fk::as_stream(stream));
 }
 
 extern "C" int fk_moe_gemm_wgrad(const void* a, int m_dim, const void* b, int n_dim,
                                  int64_t max_rows, const int* seg_start, int n_experts, void* dw,
                                  int* err_flag, void* stream) {
-  FK_CHECK_ARG(a && b && seg_start && dw && err_flag, "fk_moe_gemm_wgrad: null pointer");
-  FK_CHECK_ARG(max_rows >= 0 && max_rows % G::BM == 0, "fk_moe_gemm_wgrad: max_rows must be a multiple of 128");
-  FK_CHECK_ARG(n_experts >= 1 && n_experts <= G::kMaxGemmExperts && m_dim % 64 == 0 &&
-                   n_dim % 64 == 0 && m_dim > 0 && n_dim > 0,
-               "fk_moe_gemm_wgrad: dims must be positive multiples of 64");
-  FK_CHECK_ARG(fk::aligned16(a) && fk::aligned16(b) && fk::aligned16(dw), "fk_moe_gemm_wgrad: unaligned");
-  const int bn = G::pick_bn(n_dim);
-  int st;
-  CUtensorMap ma, mb;
-  const uint64_t rows = max_rows > 0 ? (uint64_t)max_rows : 128;
-  uint64_t da[2] = {(uint64_t)m_dim, rows}, sa[1] = {(uint64_t)m_dim * 2};
-  uint32_t ba[2] = {64, 64};
-  if ((st = G::make_map(&ma, a, 2, da, sa, ba))) return st;
-  uint64_t db[2] = {(uint64_t)n_dim, rows}, sb[1] = {(uint64_t)n_dim * 2};
-  uint32_t bb[2] = {64, 64};
-  if ((st = G::make_map(&mb, b, 2, db, sb, bb))) return st;
-  Params p{};
-  p.M = m_dim;
-  p.N = n_dim;
-  p.E = n_experts;
-  p.seg_start = seg_start;
-  p.out0 = static_cast<__nv_bfloat16*>(dw);
-  p.ld0 = n_dim;
-  p.err = err_flag;
-  const int max_tiles = n_experts * ((m_dim + G::BM - 1) / G::BM) * (n_dim / bn);
-  // TMA stores need every 128-row tile inside one expert's [m_dim, n_dim] block.
-  CUtensorMap mc0;
-  p.tma_store = (m_dim % G::BM == 0) ? 1 : 0;
-  if (p.tma_store && (st = G::make_out_map(&mc0, dw, (int64_t)n_experts * m_dim, n_dim, n_dim))) return st;
-  if (!p.tma_store) mc0 = ma;  // unused
-  cudaStream_t s = fk::as_stream(stream);
-  FK_BN_SWITCH(bn, return G::launch<BN_, true, true, G::MODE_K, G::EPI_STORE>(ma, mb, mc0, mc0, p, max_tiles, s));
-  return FK_OK;
+  return G::gemm_wgrad<G::KIND_BF16>(a, nullptr, m_dim, b, nullptr, n_dim, max_rows, seg_start,
+                                     n_experts, dw, err_flag, fk::as_stream(stream));
 }

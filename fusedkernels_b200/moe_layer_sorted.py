@@ -18,8 +18,12 @@ backward fused into the epilogue, and the per-expert weight-gradient GEMMs.
 Expert weights live in two stacked buffers, w13 [E, 2H, D] (gate rows then up rows) and
 w2 [E, D, H]; every ``experts[e].w_*.weight`` Parameter is a view into them (re-pointed at
 construction and after ``.to()``/``.cuda()``/dtype casts), so the parameters the reference
-exposes stay the leaves that receive gradients.  The tensor-core path computes in bf16:
-activations and expert weights must be bfloat16.
+exposes stay the leaves that receive gradients.
+
+Every GEMM runs on the tcgen05 tensor cores in the layer's dtype: bf16 and fp16 layers on
+16-bit MMAs with fp32 accumulation; fp32 layers (the reference's default dtype) with the
+3xTF32 split (each fp32 operand becomes a tf32 hi part plus a residual, and the kernel
+sums hi*hi + hi*lo + lo*hi in fp32), which keeps fp32-class accuracy.
 """
 import torch
 import torch.nn as nn
@@ -56,6 +60,23 @@ def _check_err(plan):
         raise RuntimeError(f"fk_moe_gemm: a pipeline wait timed out (code {e[1]})")
 
 
+def _split(t, st):
+    """fp32 tensor -> (hi, lo) for the 3xTF32 GEMMs (fk_tf32_split)."""
+    hi = torch.empty_like(t)
+    lo = torch.empty_like(t)
+    _lib.call("fk_tf32_split", t.data_ptr(), t.numel(), hi.data_ptr(), lo.data_ptr(), st)
+    return hi, lo
+
+
+def _operand(t, st):
+    """GEMM operand pair (value, lo part): fp32 operands are split, 16-bit ones are not."""
+    return _split(t, st) if t.dtype == torch.float32 else (t, None)
+
+
+def _p(t):
+    return None if t is None else t.data_ptr()
+
+
 class _SortedMoEFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, w, idx, layer, *expert_params):
@@ -63,6 +84,8 @@ class _SortedMoEFn(torch.autograd.Function):
         k = idx.shape[1]
         E, H = layer.n_experts, layer.hidden_dim
         dev = x.device
+        dt = x.dtype
+        code = _lib.dtype_code(dt)
         st = _lib.stream_of(x)
         plan = _Plan(n, k, E, dev)
         R = plan.max_rows
@@ -73,26 +96,39 @@ class _SortedMoEFn(torch.autograd.Function):
                   plan.counts.data_ptr(), plan.seg_start.data_ptr(), plan.tile_expert.data_ptr(),
                   plan.n_mblk.data_ptr(), plan.sorted_assign.data_ptr(), plan.sorted_w.data_ptr(),
                   plan.slot_pos.data_ptr(), R, plan.ws.data_ptr(), plan.ws.numel(), eptr, st)
-        bf = dict(dtype=torch.bfloat16, device=dev)
-        xs = torch.empty(R, d, **bf)
-        h1 = torch.empty(R, 2 * H, **bf)
-        act = torch.empty(R, H, **bf)
-        y = torch.empty(R, d, **bf)
-        out = torch.empty(n, d, **bf)
+        td = dict(dtype=dt, device=dev)
+        xs = torch.empty(R, d, **td)
+        h1 = torch.empty(R, 2 * H, **td)
+        act = torch.empty(R, H, **td)
+        y = torch.empty(R, d, **td)
+        out = torch.empty(n, d, **td)
+        xs_lo = act_lo = None
         if R > 0:
             _lib.call("fk_moe_gather", x.data_ptr(), d, plan.sorted_assign.data_ptr(), k,
-                      plan.n_mblk.data_ptr(), R, xs.data_ptr(), _lib.FK_BF16, st)
-            _lib.call("fk_moe_gemm_up", xs.data_ptr(), R, d, layer.w13.data_ptr(), H, E,
-                      plan.tile_expert.data_ptr(), plan.n_mblk.data_ptr(), h1.data_ptr(),
-                      act.data_ptr(), eptr + 4, st)
-            _lib.call("fk_moe_gemm_down", act.data_ptr(), R, H, layer.w2.data_ptr(), d, E,
-                      plan.tile_expert.data_ptr(), plan.n_mblk.data_ptr(), y.data_ptr(),
-                      eptr + 4, st)
+                      plan.n_mblk.data_ptr(), R, xs.data_ptr(), code, st)
+            te, nm = plan.tile_expert.data_ptr(), plan.n_mblk.data_ptr()
+            if dt == torch.bfloat16:
+                _lib.call("fk_moe_gemm_up", xs.data_ptr(), R, d, layer.w13.data_ptr(), H, E, te,
+                          nm, h1.data_ptr(), act.data_ptr(), eptr + 4, st)
+                _lib.call("fk_moe_gemm_down", act.data_ptr(), R, H, layer.w2.data_ptr(), d, E,
+                          te, nm, y.data_ptr(), eptr + 4, st)
+            else:
+                xs, xs_lo = _operand(xs, st)
+                w13, w13_lo = _operand(layer.w13, st)
+                _lib.call("fk_moe_gemm_up_typed", xs.data_ptr(), _p(xs_lo), R, d, w13.data_ptr(),
+                          _p(w13_lo), H, E, te, nm, h1.data_ptr(), act.data_ptr(), code,
+                          eptr + 4, st)
+                del w13, w13_lo
+                act, act_lo = _operand(act, st)
+                w2, w2_lo = _operand(layer.w2, st)
+                _lib.call("fk_moe_gemm_down_typed", act.data_ptr(), _p(act_lo), R, H,
+                          w2.data_ptr(), _p(w2_lo), d, E, te, nm, y.data_ptr(), code, eptr + 4, st)
         _lib.call("fk_moe_combine", y.data_ptr(), d, plan.slot_pos.data_ptr(), w.data_ptr(), n, k,
-                  out.data_ptr(), _lib.FK_BF16, st)
+                  out.data_ptr(), code, st)
         if layer.check_errors:
             _check_err(plan)
-        ctx.save_for_backward(xs, h1, act, y)
+        # fp32: xs / act are the hi parts and xs_lo / act_lo the lo parts
+        ctx.save_for_backward(xs, h1, act, y, xs_lo, act_lo)
         ctx.plan = plan
         ctx.layer = layer
         ctx.dims = (n, d, k, E, H)
@@ -100,38 +136,58 @@ class _SortedMoEFn(torch.autograd.Function):
 
     @staticmethod
     def backward(ctx, dout):
-        xs, h1, act, y = ctx.saved_tensors
+        xs, h1, act, y, xs_lo, act_lo = ctx.saved_tensors
         plan, layer = ctx.plan, ctx.layer
         n, d, k, E, H = ctx.dims
         R = plan.max_rows
         dev = xs.device
+        dt = xs.dtype
+        code = _lib.dtype_code(dt)
         st = _lib.stream_of(xs)
         eptr = plan.err.data_ptr()
-        dout = dout.to(torch.bfloat16).contiguous()
-        bf = dict(dtype=torch.bfloat16, device=dev)
-        dy = torch.empty(R, d, **bf)
+        dout = dout.to(dt).contiguous()
+        td = dict(dtype=dt, device=dev)
+        dy = torch.empty(R, d, **td)
         dw = torch.empty(n, k, dtype=torch.float32, device=dev)
-        dh1 = torch.empty(R, 2 * H, **bf)
-        dxs = torch.empty(R, d, **bf)
-        dw13 = torch.empty(E, 2 * H, d, **bf)
-        dw2 = torch.empty(E, d, H, **bf)
-        dx = torch.empty(n, d, **bf)
+        dh1 = torch.empty(R, 2 * H, **td)
+        dxs = torch.empty(R, d, **td)
+        dw13 = torch.empty(E, 2 * H, d, **td)
+        dw2 = torch.empty(E, d, H, **td)
+        dx = torch.empty(n, d, **td)
         if R > 0:
+            te, nm, seg = plan.tile_expert.data_ptr(), plan.n_mblk.data_ptr(), plan.seg_start.data_ptr()
             _lib.call("fk_moe_combine_bwd", dout.data_ptr(), y.data_ptr(), d,
                       plan.sorted_assign.data_ptr(), plan.sorted_w.data_ptr(), k,
-                      plan.n_mblk.data_ptr(), R, dy.data_ptr(), dw.data_ptr(), _lib.FK_BF16, st)
-            _lib.call("fk_moe_gemm_down_dgrad", dy.data_ptr(), R, d, layer.w2.data_ptr(), H, E,
-                      plan.tile_expert.data_ptr(), plan.n_mblk.data_ptr(), h1.data_ptr(),
-                      dh1.data_ptr(), eptr + 4, st)
-            _lib.call("fk_moe_gemm_wgrad", dy.data_ptr(), d, act.data_ptr(), H, R,
-                      plan.seg_start.data_ptr(), E, dw2.data_ptr(), eptr + 4, st)
-            _lib.call("fk_moe_gemm_up_dgrad", dh1.data_ptr(), R, H, layer.w13.data_ptr(), d, E,
-                      plan.tile_expert.data_ptr(), plan.n_mblk.data_ptr(), dxs.data_ptr(),
-                      eptr + 4, st)
-            _lib.call("fk_moe_gemm_wgrad", dh1.data_ptr(), 2 * H, xs.data_ptr(), d, R,
-                      plan.seg_start.data_ptr(), E, dw13.data_ptr(), eptr + 4, st)
+                      plan.n_mblk.data_ptr(), R, dy.data_ptr(), dw.data_ptr(), code, st)
+            if dt == torch.bfloat16:
+                _lib.call("fk_moe_gemm_down_dgrad", dy.data_ptr(), R, d, layer.w2.data_ptr(), H, E,
+                          te, nm, h1.data_ptr(), dh1.data_ptr(), eptr + 4, st)
+                _lib.call("fk_moe_gemm_wgrad", dy.data_ptr(), d, act.data_ptr(), H, R, seg, E,
+                          dw2.data_ptr(), eptr + 4, st)
+                _lib.call("fk_moe_gemm_up_dgrad", dh1.data_ptr(), R, H, layer.w13.data_ptr(), d,
+                          E, te, nm, dxs.data_ptr(), eptr + 4, st)
+                _lib.call("fk_moe_gemm_wgrad", dh1.data_ptr(), 2 * H, xs.data_ptr(), d, R, seg, E,
+                          dw13.data_ptr(), eptr + 4, st)
+            else:
+                dy, dy_lo = _operand(dy, st)
+                w2, w2_lo = _operand(layer.w2, st)
+                _lib.call("fk_moe_gemm_down_dgrad_typed", dy.data_ptr(), _p(dy_lo), R, d,
+                          w2.data_ptr(), _p(w2_lo), H, E, te, nm, h1.data_ptr(), dh1.data_ptr(),
+                          code, eptr + 4, st)
+                del w2, w2_lo
+                _lib.call("fk_moe_gemm_wgrad_typed", dy.data_ptr(), _p(dy_lo), d, act.data_ptr(),
+                          _p(act_lo), H, R, seg, E, dw2.data_ptr(), code, eptr + 4, st)
+                dh1, dh1_lo = _operand(dh1, st)
+                w13, w13_lo = _operand(layer.w13, st)
+                _lib.call("fk_moe_gemm_up_dgrad_typed", dh1.data_ptr(), _p(dh1_lo), R, H,
+                          w13.data_ptr(), _p(w13_lo), d, E, te, nm, dxs.data_ptr(), code,
+                          eptr + 4, st)
+                del w13, w13_lo
+                _lib.call("fk_moe_gemm_wgrad_typed", dh1.data_ptr(), _p(dh1_lo), 2 * H,
+                          xs.data_ptr(), _p(xs_lo), d, R, seg, E, dw13.data_ptr(), code,
+                          eptr + 4, st)
             _lib.call("fk_moe_combine", dxs.data_ptr(), d, plan.slot_pos.data_ptr(), None, n, k,
-                      dx.data_ptr(), _lib.FK_BF16, st)
+                      dx.data_ptr(), code, st)
         else:
             dw.zero_()
             dw13.zero_()
@@ -211,9 +267,11 @@ class FusedMoEMLPSorted(nn.Module):
         orig_shape = x.shape
         x_flat = x.reshape(-1, self.dim)
         self._ensure_stacked()
-        if x_flat.dtype != torch.bfloat16 or self.w13.dtype != torch.bfloat16:
-            raise TypeError("FusedMoEMLPSorted runs on bf16 tensor cores: use bfloat16 "
-                            "activations and call .bfloat16() on the layer")
+        if x_flat.dtype != self.w13.dtype:
+            raise TypeError(f"FusedMoEMLPSorted: input dtype {x_flat.dtype} does not match the "
+                            f"layer's parameters ({self.w13.dtype})")
+        if x_flat.dtype not in (torch.float32, torch.float16, torch.bfloat16):
+            raise TypeError(f"FusedMoEMLPSorted: unsupported dtype {x_flat.dtype}")
         x_flat = x_flat.contiguous()
         router_logits = self.router(x_flat)
         route_fn = fused_moe_route_v2 if self.router_version == "v2" else fused_moe_route

@@ -219,6 +219,40 @@ FK_API int fk_moe_gemm_wgrad(const void* a, int m_dim, const void* b, int n_dim,
                              int64_t max_rows, const int* seg_start, int n_experts, void* dw,
                              int* err_flag, void* stream);
 
+/* Typed variants for fp16 and fp32 layers (the reference's layers run in the caller's dtype,
+ * fp32 by default: moe_layer_sorted.py:28-37, moe_layer.py:22-31).  dtype: FK_BF16 (same as
+ * the entry points above), FK_F16 (fp16 operands and outputs, kind::f16 MMAs) or FK_F32.
+ * FK_F32 runs the 3xTF32 split on kind::tf32 MMAs: every operand X is passed as the pair
+ * (X, X_lo) produced by fk_tf32_split (X = the hi part), and the kernel accumulates
+ * A_hi*B_hi + A_hi*B_lo + A_lo*B_hi in fp32 (about 2^-21 relative error per product,
+ * fp32-class results); outputs and the SwiGLU epilogue are fp32.  The *_lo pointers are
+ * ignored for the 16-bit dtypes (pass NULL).  Same layouts and shape rules as above. */
+FK_API int fk_moe_gemm_up_typed(const void* xs, const void* xs_lo, int64_t max_rows, int dim,
+                                const void* w13, const void* w13_lo, int hidden, int n_experts,
+                                const int* tile_expert, const int* n_mblk, void* h1, void* act,
+                                int dtype, int* err_flag, void* stream);
+FK_API int fk_moe_gemm_down_typed(const void* act, const void* act_lo, int64_t max_rows,
+                                  int hidden, const void* w2, const void* w2_lo, int dim,
+                                  int n_experts, const int* tile_expert, const int* n_mblk,
+                                  void* y, int dtype, int* err_flag, void* stream);
+FK_API int fk_moe_gemm_down_dgrad_typed(const void* dy, const void* dy_lo, int64_t max_rows,
+                                        int dim, const void* w2, const void* w2_lo, int hidden,
+                                        int n_experts, const int* tile_expert, const int* n_mblk,
+                                        const void* h1, void* dh1, int dtype, int* err_flag,
+                                        void* stream);
+FK_API int fk_moe_gemm_up_dgrad_typed(const void* dh1, const void* dh1_lo, int64_t max_rows,
+                                      int hidden, const void* w13, const void* w13_lo, int dim,
+                                      int n_experts, const int* tile_expert, const int* n_mblk,
+                                      void* dxs, int dtype, int* err_flag, void* stream);
+FK_API int fk_moe_gemm_wgrad_typed(const void* a, const void* a_lo, int m_dim, const void* b,
+                                   const void* b_lo, int n_dim, int64_t max_rows,
+                                   const int* seg_start, int n_experts, void* dw, int dtype,
+                                   int* err_flag, void* stream);
+
+/* hi[i] = src[i] with its 13 low mantissa bits cleared (a tf32 value), lo[i] = src[i] - hi[i]
+ * (exact), for the fp32 GEMMs above.  src, hi, lo 16-byte aligned, n elements. */
+FK_API int fk_tf32_split(const float* src, int64_t n, float* hi, float* lo, void* stream);
+
 /* Same as fk_moe_route_meta with int32 expert ids where a negative id marks an unused
  * slot (expert-parallel receive buffers carry -1 for slots owned by other ranks). */
 FK_API int fk_moe_route_meta_skip(const int* idx, const float* w, int64_t n_tokens, int k,

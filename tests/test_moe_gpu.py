@@ -384,3 +384,203 @@ def test_masked_dispatch_layer_api():
                                              dout.reshape(-1, D).cpu())
     close(out.reshape(-1, D).cpu(), ro)
     close(dx.reshape(-1, D).cpu(), rdx + rdl @ moe.router.weight.double().cpu())
+
+
+# ----------------------------------------------------------------- fp16 / fp32 layers ---
+def _typed_operand(t, st):
+    if t.dtype != torch.float32:
+        return t, None
+    hi, lo = torch.empty_like(t), torch.empty_like(t)
+    _lib.call("fk_tf32_split", t.data_ptr(), t.numel(), hi.data_ptr(), lo.data_ptr(), st)
+    return hi, lo
+
+
+def _pp(t):
+    return None if t is None else t.data_ptr()
+
+
+def test_tf32_split_is_exact():
+    """hi has the 13 low mantissa bits cleared and hi + lo == x exactly (odd length: tail)."""
+    x = torch.randn(1001, generator=gen(8)).to(DEV) * 1e3
+    x[0], x[1], x[2] = 0.0, -0.0, 1e-40  # zeros and a denormal
+    hi, lo = torch.empty_like(x), torch.empty_like(x)
+    _lib.call("fk_tf32_split", x.data_ptr(), x.numel(), hi.data_ptr(), lo.data_ptr(),
+              torch.cuda.current_stream().cuda_stream)
+    assert torch.equal(hi + lo, x)
+    assert (hi.view(torch.int32) & 0x1FFF).eq(0).all()
+    normal = x.abs() >= torch.finfo(torch.float32).tiny
+    assert (lo.abs() <= x.abs() * 2 ** -10)[normal].all()
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.float16])
+@pytest.mark.parametrize("n,k,E,D,H", [(512, 2, 8, 256, 128), (300, 4, 16, 64, 64),
+                                       (64, 8, 128, 128, 256)])
+def test_typed_gemms_match_fp64(dtype, n, k, E, D, H):
+    """All five grouped GEMMs of the fp16 and fp32 (3xTF32) layers against fp64 matmuls of
+    the same operands: fp32 within 1e-5 of the max magnitude, fp16 within 2e-2."""
+    code = _lib.dtype_code(dtype)
+    tol = 1e-5 if dtype == torch.float32 else 2e-2
+    w, idx = random_routing(n, k, E, n + 3 * D, 0.5)
+    G = gen(n + D)
+    x = torch.randn(n, D, generator=G).to(dtype).to(DEV)
+    w13 = (torch.randn(E, 2 * H, D, generator=G) * D ** -0.5).to(dtype).to(DEV)
+    w2 = (torch.randn(E, D, H, generator=G) * H ** -0.5).to(dtype).to(DEV)
+    plan = meta(idx.to(DEV), w.to(DEV), E)
+    R = plan.max_rows
+    st = torch.cuda.current_stream().cuda_stream
+    te, nm, seg = plan.tile_expert.data_ptr(), plan.n_mblk.data_ptr(), plan.seg_start.data_ptr()
+    eptr = plan.err.data_ptr() + 4
+    xs = torch.empty(R, D, dtype=dtype, device=DEV)
+    _lib.call("fk_moe_gather", x.data_ptr(), D, plan.sorted_assign.data_ptr(), k,
+              plan.n_mblk.data_ptr(), R, xs.data_ptr(), code, st)
+    eor, rows = expert_of_rows(plan)
+    td = dict(dtype=dtype, device=DEV)
+    h1, act, y = torch.empty(R, 2 * H, **td), torch.empty(R, H, **td), torch.empty(R, D, **td)
+    xa, w13p, w2p = _typed_operand(xs, st), _typed_operand(w13, st), _typed_operand(w2, st)
+    _lib.call("fk_moe_gemm_up_typed", xa[0].data_ptr(), _pp(xa[1]), R, D, w13p[0].data_ptr(),
+              _pp(w13p[1]), H, E, te, nm, h1.data_ptr(), act.data_ptr(), code, eptr, st)
+    aa = _typed_operand(act, st)
+    _lib.call("fk_moe_gemm_down_typed", aa[0].data_ptr(), _pp(aa[1]), R, H, w2p[0].data_ptr(),
+              _pp(w2p[1]), D, E, te, nm, y.data_ptr(), code, eptr, st)
+    sa = plan.sorted_assign[:rows]
+    valid = (sa >= 0)[:, None]
+    dy = torch.where(valid, torch.randn(rows, D, generator=G).to(dtype).to(DEV), 0)
+    dyb = torch.zeros(R, D, **td)
+    dyb[:rows] = dy
+    dh1, dxs = torch.empty(R, 2 * H, **td), torch.empty(R, D, **td)
+    dw2, dw13 = torch.empty(E, D, H, **td), torch.empty(E, 2 * H, D, **td)
+    da = _typed_operand(dyb, st)
+    _lib.call("fk_moe_gemm_down_dgrad_typed", da[0].data_ptr(), _pp(da[1]), R, D,
+              w2p[0].data_ptr(), _pp(w2p[1]), H, E, te, nm, h1.data_ptr(), dh1.data_ptr(), code,
+              eptr, st)
+    _lib.call("fk_moe_gemm_wgrad_typed", da[0].data_ptr(), _pp(da[1]), D, aa[0].data_ptr(),
+              _pp(aa[1]), H, R, seg, E, dw2.data_ptr(), code, eptr, st)
+    ha = _typed_operand(dh1, st)
+    _lib.call("fk_moe_gemm_up_dgrad_typed", ha[0].data_ptr(), _pp(ha[1]), R, H,
+              w13p[0].data_ptr(), _pp(w13p[1]), D, E, te, nm, dxs.data_ptr(), code, eptr, st)
+    _lib.call("fk_moe_gemm_wgrad_typed", ha[0].data_ptr(), _pp(ha[1]), 2 * H, xa[0].data_ptr(),
+              _pp(xa[1]), D, R, seg, E, dw13.data_ptr(), code, eptr, st)
+    torch.cuda.synchronize()
+    assert plan.err[1].item() == 0
+    X = xs[:rows].double() if dtype != torch.float32 else (xa[0] + xa[1])[:rows].double()
+    ref_h1 = torch.einsum("rd,rjd->rj", X, w13.double()[eor])
+    close(h1[:rows], ref_h1, tol)
+    g, u = ref_h1[:, :H], ref_h1[:, H:]
+    close(act[:rows], F.silu(g) * u, tol)
+    A = act[:rows].double() if dtype != torch.float32 else (aa[0] + aa[1])[:rows].double()
+    close(y[:rows], torch.einsum("rh,rdh->rd", A, w2.double()[eor]), tol)
+    H1 = h1[:rows].double()
+    dact = torch.einsum("rd,rdh->rh", dy.double(), w2.double()[eor])
+    g, u = H1[:, :H], H1[:, H:]
+    s = torch.sigmoid(g)
+    ref_dh1 = torch.cat([dact * u * s * (1 + g * (1 - s)), dact * g * s], dim=1)
+    close(dh1[:rows], ref_dh1, tol)
+    DH1 = dh1[:rows].double() if dtype != torch.float32 else (ha[0] + ha[1])[:rows].double()
+    close(dxs[:rows], torch.einsum("rj,rjd->rd", DH1, w13.double()[eor]), tol)
+    segl = plan.seg_start.cpu().tolist()
+    for e in range(E):
+        a, b = segl[e], segl[e + 1]
+        if b == a:
+            assert torch.count_nonzero(dw2[e]) == 0 and torch.count_nonzero(dw13[e]) == 0
+            continue
+        close(dw2[e], dy[a:b].double().t() @ A[a:b], tol)
+        close(dw13[e], DH1[a:b].t() @ X[a:b], tol)
+
+
+def _naive_check(layer, x, k, tol, dout):
+    """Layer output, input gradient and router gradient against the fp64 oracle at the
+    reference's tolerance form: |got - ref| <= atol + rtol * |ref| elementwise."""
+    out, dx, logits = run_layer(layer, x, dout)
+    D, H = layer.dim, layer.hidden_dim
+    w13 = layer.w13.double().cpu()
+    ro, rdx, rdwg, rdwu, rdwd, rdl = moe_layer_oracle(
+        x.reshape(-1, D).cpu(), logits.cpu(), w13[:, :H], w13[:, H:], layer.w2.double().cpu(), k,
+        dout.reshape(-1, D).cpu())
+    wr = layer.router.weight.double().cpu()
+    X = x.reshape(-1, D).double().cpu()
+    torch.testing.assert_close(out.reshape(-1, D).double().cpu(), ro, atol=tol, rtol=tol)
+    torch.testing.assert_close(dx.reshape(-1, D).double().cpu(), rdx + rdl @ wr, atol=tol, rtol=tol)
+    torch.testing.assert_close(layer.router.weight.grad.double().cpu(), rdl.t() @ X, atol=tol, rtol=tol)
+    g13, g2 = stacked_grads(layer)
+    torch.testing.assert_close(g13.double().cpu(), torch.cat([rdwg, rdwu], dim=1), atol=tol, rtol=tol)
+    torch.testing.assert_close(g2.double().cpu(), rdwd, atol=tol, rtol=tol)
+
+
+@pytest.mark.parametrize("E,k", [(8, 2), (32, 4), (64, 8), (128, 16)])
+def test_layer_fp32_reference_test_shapes(E, k):
+    """tests/test_moe_sorted_dispatch.py:43-69 as the reference runs it: an fp32 layer with
+    default nn.Linear init, x [2, 128, 256], H=512, router v2; out, x.grad and the router
+    weight gradient within atol = rtol = 1e-3 (the reference test's tolerance), and the
+    expert weight gradients too."""
+    torch.manual_seed(0)
+    B, T, D, H = 2, 128, 256, 512
+    layer = FusedMoEMLPSorted(D, H, E, k, router_version="v2").cuda()
+    x = torch.randn(B, T, D, device=DEV)
+    dout = torch.randn(B, T, D, device=DEV)
+    _naive_check(layer, x, k, 1e-3, dout)
+
+
+def test_layer_fp32_matches_reference_golden(golden_moe):
+    """The reference's NaiveMoEMLP outputs (fp64 on the CPU, tests/golden/make_moe_golden.py)
+    for 64 tokens, D = H = 64, E = 8, k = 2, against the fp32 layer on the GPU: out, dx,
+    router and expert weight gradients within atol 1e-4, rtol 1e-3."""
+    g = {kk[len("moe_e8k2_"):]: torch.from_numpy(v) for kk, v in golden_moe.items()
+         if kk.startswith("moe_e8k2_")}
+    E, k = g["wg"].shape[0], int(g["k"])
+    H, D = g["wg"].shape[1], g["wg"].shape[2]
+    layer = FusedMoEMLPSorted(D, H, E, k).cuda()
+    with torch.no_grad():
+        layer.router.weight.copy_(g["wr"])
+        for e, ex in enumerate(layer.experts):
+            ex.w_gate.weight.copy_(g["wg"][e])
+            ex.w_up.weight.copy_(g["wu"][e])
+            ex.w_down.weight.copy_(g["wd"][e])
+    x = g["x"].to(DEV).requires_grad_(True)
+    out = layer(x)
+    out.backward(g["dout"].to(DEV))
+    tol = dict(atol=1e-4, rtol=1e-3)
+    torch.testing.assert_close(out.detach().cpu(), g["out"], **tol)
+    torch.testing.assert_close(x.grad.cpu(), g["dx"], **tol)
+    torch.testing.assert_close(layer.router.weight.grad.cpu(), g["dwr"], **tol)
+    g13, g2 = stacked_grads(layer)
+    torch.testing.assert_close(g13.cpu(), torch.cat([g["dwg"], g["dwu"]], dim=1), **tol)
+    torch.testing.assert_close(g2.cpu(), g["dwd"], **tol)
+
+
+def test_masked_dispatch_layer_fp32_reference_test():
+    """tests/test_moe_correctness.py:50-65 exactly: FusedMoEMLP(dim=256, hidden_dim=512,
+    n_experts=8, k=2, router_version="v1") in fp32, x [2, 64, 256]; plus values against
+    the oracle at 1e-3."""
+    from fusedkernels_b200.moe_layer import FusedMoEMLP
+    torch.manual_seed(2)
+    B, T, D = 2, 64, 256
+    moe = FusedMoEMLP(dim=D, hidden_dim=512, n_experts=8, k=2, router_version="v1").cuda()
+    x = torch.randn(B, T, D, device=DEV, requires_grad=True)
+    out = moe(x)
+    assert out.shape == x.shape
+    out.sum().backward()
+    assert x.grad is not None and x.grad.shape == x.shape
+    assert moe.router.weight.grad is not None
+    moe.zero_grad(set_to_none=True)
+    _naive_check(moe, x.detach(), 2, 1e-3, torch.randn(B, T, D, device=DEV))
+
+
+def test_layer_fp16_matches_oracle():
+    """An fp16 layer (kind::f16 MMAs with fp16 operands): outputs and gradients within 2e-2
+    of each tensor's max magnitude."""
+    torch.manual_seed(4)
+    D, H, E, k = 256, 512, 32, 4
+    layer = FusedMoEMLPSorted(D, H, E, k).to(DEV).half()
+    G = gen(9)
+    x = torch.randn(256, D, generator=G).half().to(DEV)
+    dout = torch.randn(256, D, generator=G).half().to(DEV)
+    out, dx, logits = run_layer(layer, x, dout)
+    w13 = layer.w13.float().cpu()
+    ro, rdx, rdwg, rdwu, rdwd, rdl = moe_layer_oracle(x.cpu(), logits.cpu(), w13[:, :H],
+                                                      w13[:, H:], layer.w2.float().cpu(), k,
+                                                      dout.cpu())
+    close(out.cpu(), ro)
+    close(dx.cpu(), rdx + rdl @ layer.router.weight.double().cpu())
+    g13, g2 = stacked_grads(layer)
+    close(g13.cpu(), torch.cat([rdwg, rdwu], dim=1))
+    close(g2.cpu(), rdwd)
