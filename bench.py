@@ -736,13 +736,19 @@ class MoELayer(Workload):
         return moe_cpu_sample(self, 256)
 
     def config(self):
-        par = "single GPU" if self.world == 1 else (
-            f"ep{self.world}: {len(self.replicated)} hot experts replicated on every GPU "
-            f"(gradients all-reduced), the other {self.E - len(self.replicated)} placed by "
-            f"load-aware LPT bin packing (placement and replicated set from a calibration "
-            f"batch, seed 1; the timed batch is seed 0), dispatch/combine "
-            + ("by put kernels into peer memory over NVLink" if self.ep_transport == "peer"
-               else "by NCCL all-to-all") + f"; {self.tokens // self.world} tokens per GPU")
+        if getattr(self, "host_only", False):
+            # reference arm: the oracle on the host cores, whatever the GPU count
+            par = "host CPU cores (reference path; no GPU, no expert sharding)"
+        elif self.world == 1:
+            par = "single GPU"
+        else:
+            par = (
+                f"ep{self.world}: {len(self.replicated)} hot experts replicated on every GPU "
+                f"(gradients all-reduced), the other {self.E - len(self.replicated)} placed by "
+                f"load-aware LPT bin packing (placement and replicated set from a calibration "
+                f"batch, seed 1; the timed batch is seed 0), dispatch/combine "
+                + ("by put kernels into peer memory over NVLink" if self.ep_transport == "peer"
+                   else "by NCCL all-to-all") + f"; {self.tokens // self.world} tokens per GPU")
         return {"workload": "moe_sorted_dispatch_fwd_bwd", "tokens": self.tokens, "dim": self.dim,
                 "hidden": self.hidden, "n_experts": self.E, "k": self.k, "dtype": "bf16",
                 "router_bias": "2*ln(zipf(1.1) rank weights)", "parallelism": par,
@@ -961,7 +967,9 @@ def run_reference(args):
     value = units / dt
     out = {"metric": wl.metric, "value": value, "unit": wl.unit, "n_gpus": int(os.environ.get("WORLD_SIZE", "1")),
            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt * 1e3, 3),
-           "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+           "higher_is_better": True,
+           "scaling": "strong" if getattr(wl, "strong", False) else "weak", "vs_baseline": None,
+           "dtype": "f32",
            "data": "synthetic (seeded torch.randn, shapes of the workload)", "impl": "reference",
            "config": wl.config(),
            "cpu_baseline": {"value": value, "unit": wl.unit, "cores": cores, "kind": "port",
@@ -1079,6 +1087,8 @@ def wl_setup_host(wl):
             return time.perf_counter() - t0, (R * C * 2 * 2 + R * 8) / 1e9, \
                 f"{R} of {wl.rows} rows x {C} per step, fp32 cross-entropy fwd+bwd"
     elif isinstance(wl, MoELayer):
+        wl.host_only = True
+
         def once():
             return moe_cpu_sample(wl, 128)
     elif isinstance(wl, Router):
