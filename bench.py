@@ -572,6 +572,7 @@ class MoELayer(Workload):
     metric = "MoE layer fwd+bwd throughput"
     ep_transport = "peer"
     ep_replicate = "auto"
+    ep_overlap_sms = 16
     unit = "tokens/s"
     strong = True  # the 32768 global tokens are split across ranks
     tokens, dim, hidden, E, k = 32768, 4096, 1024, 128, 8
@@ -622,7 +623,8 @@ class MoELayer(Workload):
             self.placement = lpt_placement_excluding(load.tolist(), self.world, self.replicated)
             layer = ExpertParallelMoEMLP(D, H, E, self.k, placement=self.placement,
                                          transport=self.ep_transport,
-                                         replicated=self.replicated).to(dev).bfloat16()
+                                         replicated=self.replicated,
+                                         overlap_sms=self.ep_overlap_sms).to(dev).bfloat16()
             layer.load_from_full(wr, wg, wu, wd)
             per = self.tokens // self.world
             T0, T1 = self.rank * per, (self.rank + 1) * per
@@ -669,14 +671,15 @@ class MoELayer(Workload):
         p = self.kp
         self.lib.call("fk_moe_gemm_up", self.kxs.data_ptr(), p.max_rows, self.dim,
                       self.layer.w13.data_ptr(), self.hidden, self.E, p.tile_expert.data_ptr(),
-                      p.n_mblk.data_ptr(), self.kh1.data_ptr(), self.kact.data_ptr(),
+                      p.n_mblk.data_ptr(), self.kh1.data_ptr(), self.kact.data_ptr(), 0,
                       p.err.data_ptr() + 4, cur_stream())
 
     def gemm_down(self):
         p = self.kp
         self.lib.call("fk_moe_gemm_down", self.kact.data_ptr(), p.max_rows, self.hidden,
                       self.layer.w2.data_ptr(), self.dim, self.E, p.tile_expert.data_ptr(),
-                      p.n_mblk.data_ptr(), self.ky.data_ptr(), p.err.data_ptr() + 4, cur_stream())
+                      p.n_mblk.data_ptr(), self.ky.data_ptr(), 0, p.err.data_ptr() + 4,
+                      cur_stream())
 
     def step(self):
         self.layer.zero_grad(set_to_none=True)
@@ -744,7 +747,9 @@ class MoELayer(Workload):
         else:
             par = (
                 f"ep{self.world}: {len(self.replicated)} hot experts replicated on every GPU "
-                f"(gradients all-reduced), the other {self.E - len(self.replicated)} placed by "
+                f"(gradients all-reduced beside the input-gradient GEMMs, which leave "
+                f"{self.ep_overlap_sms} SMs to it), the other {self.E - len(self.replicated)} "
+                f"placed by "
                 f"load-aware LPT bin packing (placement and replicated set from a calibration "
                 f"batch, seed 1; the timed batch is seed 0), dispatch/combine "
                 + ("by put kernels into peer memory over NVLink" if self.ep_transport == "peer"
@@ -830,6 +835,7 @@ def run_ours(args):
     if args.workload == "moe":
         wl.ep_transport = args.ep_transport
         wl.ep_replicate = args.ep_replicate
+        wl.ep_overlap_sms = args.ep_overlap_sms
         if args.moe_tokens:
             wl.tokens = args.moe_tokens
         if args.moe_experts:
@@ -994,6 +1000,7 @@ def run_breakdown(args, reps=5):
     if args.workload == "moe":
         wl.ep_transport = args.ep_transport
         wl.ep_replicate = args.ep_replicate
+        wl.ep_overlap_sms = args.ep_overlap_sms
     wl.setup(dev)
     for _ in range(max(args.warmup, 3)):
         wl.step()
@@ -1126,6 +1133,9 @@ def main():
     ap.add_argument("--ep-replicate", choices=["auto", "none"], default="auto",
                     help="auto: replicate the experts hot enough that nearly every token picks "
                          "them on every GPU; none: exactly E/N experts per GPU")
+    ap.add_argument("--ep-overlap-sms", type=int, default=16,
+                    help="SMs the expert-parallel backward GEMMs leave free for the replicated "
+                         "experts' gradient all-reduce running beside them (N > 1)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--breakdown", action="store_true",
                     help="print the device time of every C-ABI call in one step (eager, CUDA "

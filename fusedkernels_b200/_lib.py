@@ -40,11 +40,12 @@ SIGNATURES: dict[str, list] = {
     "fk_moe_gather": [_vp, _i32, _vp, _i32, _vp, _i64, _vp, _i32, _vp],
     "fk_moe_combine": [_vp, _i32, _vp, _vp, _i64, _i32, _vp, _i32, _vp],
     "fk_moe_combine_bwd": [_vp, _vp, _i32, _vp, _vp, _i32, _vp, _i64, _vp, _vp, _i32, _vp],
-    "fk_moe_gemm_up": [_vp, _i64, _i32, _vp, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp],
-    "fk_moe_gemm_down": [_vp, _i64, _i32, _vp, _i32, _i32, _vp, _vp, _vp, _vp, _vp],
-    "fk_moe_gemm_down_dgrad": [_vp, _i64, _i32, _vp, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp],
-    "fk_moe_gemm_up_dgrad": [_vp, _i64, _i32, _vp, _i32, _i32, _vp, _vp, _vp, _vp, _vp],
-    "fk_moe_gemm_wgrad": [_vp, _i32, _vp, _i32, _i64, _vp, _i32, _vp, _vp, _vp],
+    "fk_moe_gemm_up": [_vp, _i64, _i32, _vp, _i32, _i32, _vp, _vp, _vp, _vp, _i32, _vp, _vp],
+    "fk_moe_gemm_down": [_vp, _i64, _i32, _vp, _i32, _i32, _vp, _vp, _vp, _i32, _vp, _vp],
+    "fk_moe_gemm_down_dgrad": [_vp, _i64, _i32, _vp, _i32, _i32, _vp, _vp, _vp, _vp, _i32, _vp,
+                               _vp],
+    "fk_moe_gemm_up_dgrad": [_vp, _i64, _i32, _vp, _i32, _i32, _vp, _vp, _vp, _i32, _vp, _vp],
+    "fk_moe_gemm_wgrad": [_vp, _i32, _vp, _i32, _i64, _vp, _i32, _vp, _i32, _vp, _vp],
     "fk_tf32_split": [_vp, _i64, _vp, _vp, _vp],
     "fk_moe_gemm_up_typed": [_vp, _vp, _i64, _i32, _vp, _vp, _i32, _i32, _vp, _vp, _vp, _vp,
                              _i32, _vp, _vp],
@@ -166,3 +167,10 @@ def moe_capacity(n_tokens: int, k: int, n_experts: int) -> tuple[int, int]:
               "fk_moe_capacity")
         v = _cap_cache[key] = (rows.value, ws.value)
     return v
+
+
+def num_sms(device: torch.device | None = None) -> int:
+    """Streaming multiprocessors of the current (or given) CUDA device: the grid of the
+    persistent kernels, one CTA per SM."""
+    dev = torch.cuda.current_device() if device is None else device
+    return torch.cuda.get_device_properties(dev).multi_processor_count

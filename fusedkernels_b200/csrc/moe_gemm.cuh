@@ -664,7 +664,7 @@ constexpr CUtensorMapSwizzle mn_swizzle() {
 template <int BN, bool A_MN, bool B_MN, int MODE, int EPI, int KIND>
 int launch(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& c0,
            const CUtensorMap& c1, const CUtensorMap& a2, const CUtensorMap& b2, const Params& p,
-           int max_tiles, cudaStream_t st) {
+           int max_tiles, cudaStream_t st, int max_ctas) {
   constexpr bool kRing = sizeof(typename KindT<KIND>::T) == 2;
   constexpr int STAGE_BYTES = (BM + BN) * 128;
   constexpr int STAGES = (BN == 256) ? 4 : (BN == 128 ? 6 : 8);
@@ -672,6 +672,7 @@ int launch(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& c0,
   auto k = moe_gemm_kernel<BN, STAGES, A_MN, B_MN, MODE, EPI, KIND>;
   cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
   int grid = num_sms();
+  if (max_ctas > 0 && max_ctas < grid) grid = max_ctas;  // SMs left to concurrent work
   if (max_tiles < grid) grid = max_tiles < 1 ? 1 : max_tiles;
   k<<<grid, kThreads, SMEM, st>>>(a, b, c0, c1, a2, b2, p);
   return launch_status("fk_moe_gemm");
@@ -728,7 +729,8 @@ inline int check_lo(const void* a2, const void* b2) {
 template <int KIND>
 int gemm_up(const void* xs, const void* xs2, int64_t max_rows, int dim, const void* w13,
             const void* w132, int hidden, int n_experts, const int* tile_expert,
-            const int* n_mblk, void* h1, void* act, int* err_flag, cudaStream_t s) {
+            const int* n_mblk, void* h1, void* act, int* err_flag, cudaStream_t s,
+            int max_ctas = 0) {
   using KT = KindT<KIND>;
   constexpr int ES = sizeof(typename KT::T);
   int st = check_common(xs, w13, tile_expert, n_mblk, max_rows, n_experts);
@@ -774,15 +776,16 @@ int gemm_up(const void* xs, const void* xs2, int64_t max_rows, int dim, const vo
   }
   if constexpr (KIND == KIND_BF16) {
     if (bn == 256)
-      return launch<256, false, false, MODE_M, EPI_SWIGLU_FWD, KIND>(ma, mb, mc0, mc1, ma2, mb2, p, max_tiles, s);
+      return launch<256, false, false, MODE_M, EPI_SWIGLU_FWD, KIND>(ma, mb, mc0, mc1, ma2, mb2, p, max_tiles, s, max_ctas);
   }
-  return launch<128, false, false, MODE_M, EPI_SWIGLU_FWD, KIND>(ma, mb, mc0, mc1, ma2, mb2, p, max_tiles, s);
+  return launch<128, false, false, MODE_M, EPI_SWIGLU_FWD, KIND>(ma, mb, mc0, mc1, ma2, mb2, p, max_tiles, s, max_ctas);
 }
 
 template <int KIND>
 int gemm_down(const void* act, const void* act2, int64_t max_rows, int hidden, const void* w2,
               const void* w22, int dim, int n_experts, const int* tile_expert, const int* n_mblk,
-              void* y, int* err_flag, cudaStream_t s) {
+              void* y, int* err_flag, cudaStream_t s,
+            int max_ctas = 0) {
   using KT = KindT<KIND>;
   constexpr int ES = sizeof(typename KT::T);
   int st = check_common(act, w2, tile_expert, n_mblk, max_rows, n_experts);
@@ -822,9 +825,9 @@ int gemm_down(const void* act, const void* act2, int64_t max_rows, int hidden, c
   p.tma_store = ES == 2 ? 1 : 0;
   if (p.tma_store && (st = make_out_map<KIND>(&mc0, y, max_rows, dim, dim))) return st;
   if constexpr (KIND == KIND_BF16) {
-    FK_BN_SWITCH(bn, return (launch<BN_, false, false, MODE_M, EPI_STORE, KIND>(ma, mb, mc0, mc0, ma2, mb2, p, max_tiles, s)));
+    FK_BN_SWITCH(bn, return (launch<BN_, false, false, MODE_M, EPI_STORE, KIND>(ma, mb, mc0, mc0, ma2, mb2, p, max_tiles, s, max_ctas)));
   } else {
-    FK_BN_SWITCH_SMALL(bn, return (launch<BN_, false, false, MODE_M, EPI_STORE, KIND>(ma, mb, mc0, mc0, ma2, mb2, p, max_tiles, s)));
+    FK_BN_SWITCH_SMALL(bn, return (launch<BN_, false, false, MODE_M, EPI_STORE, KIND>(ma, mb, mc0, mc0, ma2, mb2, p, max_tiles, s, max_ctas)));
   }
   return FK_OK;
 }
@@ -832,7 +835,8 @@ int gemm_down(const void* act, const void* act2, int64_t max_rows, int hidden, c
 template <int KIND>
 int gemm_down_dgrad(const void* dy, const void* dy2, int64_t max_rows, int dim, const void* w2,
                     const void* w22, int hidden, int n_experts, const int* tile_expert,
-                    const int* n_mblk, const void* h1, void* dh1, int* err_flag, cudaStream_t s) {
+                    const int* n_mblk, const void* h1, void* dh1, int* err_flag, cudaStream_t s,
+            int max_ctas = 0) {
   using KT = KindT<KIND>;
   constexpr int ES = sizeof(typename KT::T);
   int st = check_common(dy, w2, tile_expert, n_mblk, max_rows, n_experts);
@@ -875,9 +879,9 @@ int gemm_down_dgrad(const void* dy, const void* dy2, int64_t max_rows, int dim, 
   p.tma_store = ES == 2 ? 1 : 0;
   if (p.tma_store && (st = make_out_map<KIND>(&mc0, dh1, max_rows, 2 * hidden, 2 * hidden))) return st;
   if constexpr (KIND == KIND_BF16) {
-    FK_BN_SWITCH(bn, return (launch<BN_, false, true, MODE_M, EPI_SWIGLU_BWD, KIND>(ma, mb, mc0, mc0, ma2, mb2, p, max_tiles, s)));
+    FK_BN_SWITCH(bn, return (launch<BN_, false, true, MODE_M, EPI_SWIGLU_BWD, KIND>(ma, mb, mc0, mc0, ma2, mb2, p, max_tiles, s, max_ctas)));
   } else {
-    FK_BN_SWITCH_SMALL(bn, return (launch<BN_, false, true, MODE_M, EPI_SWIGLU_BWD, KIND>(ma, mb, mc0, mc0, ma2, mb2, p, max_tiles, s)));
+    FK_BN_SWITCH_SMALL(bn, return (launch<BN_, false, true, MODE_M, EPI_SWIGLU_BWD, KIND>(ma, mb, mc0, mc0, ma2, mb2, p, max_tiles, s, max_ctas)));
   }
   return FK_OK;
 }
@@ -885,7 +889,8 @@ int gemm_down_dgrad(const void* dy, const void* dy2, int64_t max_rows, int dim, 
 template <int KIND>
 int gemm_up_dgrad(const void* dh1, const void* dh12, int64_t max_rows, int hidden, const void* w13,
                   const void* w132, int dim, int n_experts, const int* tile_expert,
-                  const int* n_mblk, void* dxs, int* err_flag, cudaStream_t s) {
+                  const int* n_mblk, void* dxs, int* err_flag, cudaStream_t s,
+            int max_ctas = 0) {
   using KT = KindT<KIND>;
   constexpr int ES = sizeof(typename KT::T);
   int st = check_common(dh1, w13, tile_expert, n_mblk, max_rows, n_experts);
@@ -926,9 +931,9 @@ int gemm_up_dgrad(const void* dh1, const void* dh12, int64_t max_rows, int hidde
   p.tma_store = ES == 2 ? 1 : 0;
   if (p.tma_store && (st = make_out_map<KIND>(&mc0, dxs, max_rows, dim, dim))) return st;
   if constexpr (KIND == KIND_BF16) {
-    FK_BN_SWITCH(bn, return (launch<BN_, false, true, MODE_M, EPI_STORE, KIND>(ma, mb, mc0, mc0, ma2, mb2, p, max_tiles, s)));
+    FK_BN_SWITCH(bn, return (launch<BN_, false, true, MODE_M, EPI_STORE, KIND>(ma, mb, mc0, mc0, ma2, mb2, p, max_tiles, s, max_ctas)));
   } else {
-    FK_BN_SWITCH_SMALL(bn, return (launch<BN_, false, true, MODE_M, EPI_STORE, KIND>(ma, mb, mc0, mc0, ma2, mb2, p, max_tiles, s)));
+    FK_BN_SWITCH_SMALL(bn, return (launch<BN_, false, true, MODE_M, EPI_STORE, KIND>(ma, mb, mc0, mc0, ma2, mb2, p, max_tiles, s, max_ctas)));
   }
   return FK_OK;
 }
@@ -936,7 +941,7 @@ int gemm_up_dgrad(const void* dh1, const void* dh12, int64_t max_rows, int hidde
 template <int KIND>
 int gemm_wgrad(const void* a, const void* a2, int m_dim, const void* b, const void* b2, int n_dim,
                int64_t max_rows, const int* seg_start, int n_experts, void* dw, int* err_flag,
-               cudaStream_t s) {
+               cudaStream_t s, int max_ctas = 0) {
   using KT = KindT<KIND>;
   constexpr int ES = sizeof(typename KT::T);
   FK_CHECK_ARG(a && b && seg_start && dw && err_flag, "fk_moe_gemm_wgrad: null pointer");
@@ -976,9 +981,9 @@ int gemm_wgrad(const void* a, const void* a2, int m_dim, const void* b, const vo
   p.tma_store = (ES == 2 && m_dim % BM == 0) ? 1 : 0;
   if (p.tma_store && (st = make_out_map<KIND>(&mc0, dw, (int64_t)n_experts * m_dim, n_dim, n_dim))) return st;
   if constexpr (KIND == KIND_BF16) {
-    FK_BN_SWITCH(bn, return (launch<BN_, true, true, MODE_K, EPI_STORE, KIND>(ma, mb, mc0, mc0, ma2, mb2, p, max_tiles, s)));
+    FK_BN_SWITCH(bn, return (launch<BN_, true, true, MODE_K, EPI_STORE, KIND>(ma, mb, mc0, mc0, ma2, mb2, p, max_tiles, s, max_ctas)));
   } else {
-    FK_BN_SWITCH_SMALL(bn, return (launch<BN_, true, true, MODE_K, EPI_STORE, KIND>(ma, mb, mc0, mc0, ma2, mb2, p, max_tiles, s)));
+    FK_BN_SWITCH_SMALL(bn, return (launch<BN_, true, true, MODE_K, EPI_STORE, KIND>(ma, mb, mc0, mc0, ma2, mb2, p, max_tiles, s, max_ctas)));
   }
   return FK_OK;
 }

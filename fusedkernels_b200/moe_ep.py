@@ -9,7 +9,8 @@ module shards the experts of ``FusedMoEMLPSorted`` across the ranks of a process
             the received rows -> per-row pre-reduction of the local slots -> partial rows
             back -> fk_ep_unpack_sum (rank-ordered sum: deterministic)
   backward  the mirror image: dout rows out, per-slot routing gradients and partial input
-            gradients back; the return exchange overlaps the weight-gradient GEMMs.
+            gradients back; the return exchange overlaps the weight-gradient GEMMs, and the
+            replicated experts' gradient all-reduce overlaps the input-gradient GEMMs.
 
 Every (source, destination) pair has a fixed capacity of T rows (a token is sent at most
 once per destination), so no host synchronisation or split-size exchange is needed.
@@ -280,9 +281,10 @@ class _EPMoEFn(torch.autograd.Function):
                   plan.n_mblk.data_ptr(), R, xs.data_ptr(), _lib.FK_BF16, st)
         _lib.call("fk_moe_gemm_up", xs.data_ptr(), R, d, layer.w13.data_ptr(), H, El,
                   plan.tile_expert.data_ptr(), plan.n_mblk.data_ptr(), h1.data_ptr(),
-                  act.data_ptr(), eptr + 4, st)
+                  act.data_ptr(), 0, eptr + 4, st)
         _lib.call("fk_moe_gemm_down", act.data_ptr(), R, H, layer.w2.data_ptr(), d, El,
-                  plan.tile_expert.data_ptr(), plan.n_mblk.data_ptr(), y.data_ptr(), eptr + 4, st)
+                  plan.tile_expert.data_ptr(), plan.n_mblk.data_ptr(), y.data_ptr(), 0, eptr + 4,
+                  st)
         if px is not None:
             _lib.call("fk_ep_peer_combine_put", y.data_ptr(), d, plan.slot_pos.data_ptr(), recv_w_p,
                       T, N, ex.rank, k, None, px.table("to_source"), None, px.table("flags"),
@@ -337,15 +339,43 @@ class _EPMoEFn(torch.autograd.Function):
         dxs = torch.empty(R, d, **bf)
         dw13 = torch.empty(El, 2 * H, d, **bf)
         dw2 = torch.empty(El, d, H, **bf)
+        te, nm = plan.tile_expert.data_ptr(), plan.n_mblk.data_ptr()
+        seg = plan.seg_start.data_ptr()
         _lib.call("fk_moe_combine_bwd", recv_d_p, y.data_ptr(), d,
                   plan.sorted_assign.data_ptr(), plan.sorted_w.data_ptr(), k,
                   plan.n_mblk.data_ptr(), R, dy.data_ptr(), dw_recv.data_ptr(), _lib.FK_BF16, st)
+
+        def wgrad(lo, hi, cap, which):
+            """Weight gradients of stacked experts lo..hi-1 (dW2 or dW13)."""
+            if hi <= lo:
+                return
+            if which == 2:
+                _lib.call("fk_moe_gemm_wgrad", dy.data_ptr(), d, act.data_ptr(), H, R,
+                          seg + 4 * lo, hi - lo, dw2[lo].data_ptr(), cap, eptr + 4, st)
+            else:
+                _lib.call("fk_moe_gemm_wgrad", dh1.data_ptr(), 2 * H, xs.data_ptr(), d, R,
+                          seg + 4 * lo, hi - lo, dw13[lo].data_ptr(), cap, eptr + 4, st)
+
+        # Replicated experts sit at the end of the stack.  Their weight gradients are
+        # computed as soon as their inputs exist (dW2 right after dy, dW13 right after dh1)
+        # and summed over the group by NCCL on its own stream, while the remaining GEMMs
+        # run on a grid that leaves layer.overlap_sms SMs free for the collective.
+        n_own = layer.n_owned
+        rep = bool(layer.replicated) and N > 1
+        cap = max(_lib.num_sms() - layer.overlap_sms, 1) if rep and layer.overlap_sms > 0 else 0
+        red = []
+        if rep:
+            wgrad(n_own, El, 0, 2)
+            red.append(dist.all_reduce(dw2[n_own:], group=ex.group, async_op=True))
         _lib.call("fk_moe_gemm_down_dgrad", dy.data_ptr(), R, d, layer.w2.data_ptr(), H, El,
-                  plan.tile_expert.data_ptr(), plan.n_mblk.data_ptr(), h1.data_ptr(),
-                  dh1.data_ptr(), eptr + 4, st)
+                  te, nm, h1.data_ptr(), dh1.data_ptr(), cap, eptr + 4, st)
+        if rep:
+            wgrad(n_own, El, cap, 13)
+            red.append(dist.all_reduce(dw13[n_own:], group=ex.group, async_op=True))
         _lib.call("fk_moe_gemm_up_dgrad", dh1.data_ptr(), R, H, layer.w13.data_ptr(), d, El,
-                  plan.tile_expert.data_ptr(), plan.n_mblk.data_ptr(), dxs.data_ptr(), eptr + 4, st)
-        # The input-gradient and routing-gradient exchange overlaps the weight-gradient GEMMs.
+                  te, nm, dxs.data_ptr(), cap, eptr + 4, st)
+        # The input-gradient and routing-gradient exchange overlaps the owned experts'
+        # weight-gradient GEMMs.
         if px is not None:
             _lib.call("fk_ep_peer_combine_put", dxs.data_ptr(), d, plan.slot_pos.data_ptr(), None,
                       T, N, ex.rank, k, dw_recv.data_ptr(), px.table("to_source"),
@@ -357,25 +387,11 @@ class _EPMoEFn(torch.autograd.Function):
                       k, dx_part.data_ptr(), _lib.FK_BF16, st)
             back_dx, w1 = ex.all_to_all(dx_part, async_op=True)
             back_dw, w2 = ex.all_to_all(dw_recv, async_op=True)
-        # Replicated experts sit at the end of the stack: their gradients are computed first
-        # and summed over the group while the owned experts' gradients are computed.
-        n_own = layer.n_owned
-        seg = plan.seg_start
-        parts = [(n_own, El), (0, n_own)] if layer.replicated and N > 1 else [(0, El)]
-        red = None
-        for lo, hi in parts:
-            if hi <= lo:
-                continue
-            _lib.call("fk_moe_gemm_wgrad", dy.data_ptr(), d, act.data_ptr(), H, R,
-                      seg.data_ptr() + 4 * lo, hi - lo, dw2[lo].data_ptr(), eptr + 4, st)
-            _lib.call("fk_moe_gemm_wgrad", dh1.data_ptr(), 2 * H, xs.data_ptr(), d, R,
-                      seg.data_ptr() + 4 * lo, hi - lo, dw13[lo].data_ptr(), eptr + 4, st)
-            if lo == n_own and hi > lo:
-                red = [dist.all_reduce(dw13[lo:hi], group=ex.group, async_op=True),
-                       dist.all_reduce(dw2[lo:hi], group=ex.group, async_op=True)]
-        if red is not None:
-            for wk in red:
-                wk.wait()
+        own_hi = n_own if rep else El
+        wgrad(0, own_hi, cap, 2)
+        wgrad(0, own_hi, cap, 13)
+        for wk in red:
+            wk.wait()
         if px is not None:
             px.wait(px.PHASE_BWD_COMBINE, st)
             back_dx_p, back_dw_p = px.local("to_source"), px.local("dw")
@@ -402,12 +418,17 @@ class ExpertParallelMoEMLP(nn.Module):
     experts held by every rank (their slots are computed on the token's own rank; their
     weight gradients are summed over the group inside backward, so every copy receives
     the full-batch gradient); their placement entries are ignored.  Every rank must
-    construct the layer with the same placement and replicated set."""
+    construct the layer with the same placement and replicated set.
+
+    overlap_sms: SMs the backward GEMMs leave free while the replicated experts' gradient
+    all-reduce runs beside them (0: the GEMMs take every SM and the collective waits)."""
 
     def __init__(self, dim: int, hidden_dim: int, n_experts: int, k: int = 2, group=None,
                  placement=None, router_version: str = "v2", transport: str = "peer",
-                 replicated=()):
+                 replicated=(), overlap_sms: int = 16):
         super().__init__()
+        assert overlap_sms >= 0
+        self.overlap_sms = int(overlap_sms)
         assert router_version == "v2"
         assert transport in ("peer", "nccl")
         self.transport = transport

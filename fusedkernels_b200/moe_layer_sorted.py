@@ -109,9 +109,9 @@ class _SortedMoEFn(torch.autograd.Function):
             te, nm = plan.tile_expert.data_ptr(), plan.n_mblk.data_ptr()
             if dt == torch.bfloat16:
                 _lib.call("fk_moe_gemm_up", xs.data_ptr(), R, d, layer.w13.data_ptr(), H, E, te,
-                          nm, h1.data_ptr(), act.data_ptr(), eptr + 4, st)
+                          nm, h1.data_ptr(), act.data_ptr(), 0, eptr + 4, st)
                 _lib.call("fk_moe_gemm_down", act.data_ptr(), R, H, layer.w2.data_ptr(), d, E,
-                          te, nm, y.data_ptr(), eptr + 4, st)
+                          te, nm, y.data_ptr(), 0, eptr + 4, st)
             else:
                 xs, xs_lo = _operand(xs, st)
                 w13, w13_lo = _operand(layer.w13, st)
@@ -161,13 +161,13 @@ class _SortedMoEFn(torch.autograd.Function):
                       plan.n_mblk.data_ptr(), R, dy.data_ptr(), dw.data_ptr(), code, st)
             if dt == torch.bfloat16:
                 _lib.call("fk_moe_gemm_down_dgrad", dy.data_ptr(), R, d, layer.w2.data_ptr(), H, E,
-                          te, nm, h1.data_ptr(), dh1.data_ptr(), eptr + 4, st)
+                          te, nm, h1.data_ptr(), dh1.data_ptr(), 0, eptr + 4, st)
                 _lib.call("fk_moe_gemm_wgrad", dy.data_ptr(), d, act.data_ptr(), H, R, seg, E,
-                          dw2.data_ptr(), eptr + 4, st)
+                          dw2.data_ptr(), 0, eptr + 4, st)
                 _lib.call("fk_moe_gemm_up_dgrad", dh1.data_ptr(), R, H, layer.w13.data_ptr(), d,
-                          E, te, nm, dxs.data_ptr(), eptr + 4, st)
+                          E, te, nm, dxs.data_ptr(), 0, eptr + 4, st)
                 _lib.call("fk_moe_gemm_wgrad", dh1.data_ptr(), 2 * H, xs.data_ptr(), d, R, seg, E,
-                          dw13.data_ptr(), eptr + 4, st)
+                          dw13.data_ptr(), 0, eptr + 4, st)
             else:
                 dy, dy_lo = _operand(dy, st)
                 w2, w2_lo = _operand(layer.w2, st)

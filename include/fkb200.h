@@ -200,24 +200,28 @@ FK_API int fk_moe_combine_bwd(const void* dout, const void* y, int dim,
  * fk_moe_gemm_up_dgrad:   dxs = dh1 @ w13[e] ([max_rows, D]).
  * fk_moe_gemm_wgrad: dw[e] = a[seg_e]^T @ b[seg_e] for every expert e ([E, m_dim, n_dim]),
  *                   a [max_rows, m_dim], b [max_rows, n_dim] (zero for empty experts).
+ * Each kernel is persistent: one CTA per SM walks the tiles.  max_ctas = 0 keeps that; a
+ * positive max_ctas caps the grid, leaving the other SMs free for work on another stream
+ * (the expert-parallel layer runs a gradient all-reduce beside its backward GEMMs).
  * Together they replace the per-expert cuBLAS calls of moe_layer_sorted.py:70-77 and
  * their autograd backward. */
 FK_API int fk_moe_gemm_up(const void* xs, int64_t max_rows, int dim, const void* w13,
                           int hidden, int n_experts, const int* tile_expert, const int* n_mblk,
-                          void* h1, void* act, int* err_flag, void* stream);
+                          void* h1, void* act, int max_ctas, int* err_flag, void* stream);
 FK_API int fk_moe_gemm_down(const void* act, int64_t max_rows, int hidden, const void* w2,
                             int dim, int n_experts, const int* tile_expert, const int* n_mblk,
-                            void* y, int* err_flag, void* stream);
+                            void* y, int max_ctas, int* err_flag, void* stream);
 FK_API int fk_moe_gemm_down_dgrad(const void* dy, int64_t max_rows, int dim, const void* w2,
                                   int hidden, int n_experts, const int* tile_expert,
-                                  const int* n_mblk, const void* h1, void* dh1, int* err_flag,
-                                  void* stream);
+                                  const int* n_mblk, const void* h1, void* dh1, int max_ctas,
+                                  int* err_flag, void* stream);
 FK_API int fk_moe_gemm_up_dgrad(const void* dh1, int64_t max_rows, int hidden, const void* w13,
                                 int dim, int n_experts, const int* tile_expert,
-                                const int* n_mblk, void* dxs, int* err_flag, void* stream);
+                                const int* n_mblk, void* dxs, int max_ctas, int* err_flag,
+                                void* stream);
 FK_API int fk_moe_gemm_wgrad(const void* a, int m_dim, const void* b, int n_dim,
                              int64_t max_rows, const int* seg_start, int n_experts, void* dw,
-                             int* err_flag, void* stream);
+                             int max_ctas, int* err_flag, void* stream);
 
 /* Typed variants for fp16 and fp32 layers (the reference's layers run in the caller's dtype,
  * fp32 by default: moe_layer_sorted.py:28-37, moe_layer.py:22-31).  dtype: FK_BF16 (same as
@@ -226,7 +230,8 @@ FK_API int fk_moe_gemm_wgrad(const void* a, int m_dim, const void* b, int n_dim,
  * (X, X_lo) produced by fk_tf32_split (X = the hi part), and the kernel accumulates
  * A_hi*B_hi + A_hi*B_lo + A_lo*B_hi in fp32 (about 2^-21 relative error per product,
  * fp32-class results); outputs and the SwiGLU epilogue are fp32.  The *_lo pointers are
- * ignored for the 16-bit dtypes (pass NULL).  Same layouts and shape rules as above. */
+ * ignored for the 16-bit dtypes (pass NULL).  Same layouts and shape rules as above; one
+ * CTA per SM. */
 FK_API int fk_moe_gemm_up_typed(const void* xs, const void* xs_lo, int64_t max_rows, int dim,
                                 const void* w13, const void* w13_lo, int hidden, int n_experts,
                                 const int* tile_expert, const int* n_mblk, void* h1, void* act,

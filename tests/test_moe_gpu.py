@@ -127,9 +127,10 @@ def test_gather_and_gemm_up_down(n, k, E, D, H):
     eptr = plan.err.data_ptr() + 4
     _lib.call("fk_moe_gemm_up", xs.data_ptr(), R, D, P["w13"].data_ptr(), H, E,
               plan.tile_expert.data_ptr(), plan.n_mblk.data_ptr(), h1.data_ptr(), act.data_ptr(),
-              eptr, P["st"])
+              0, eptr, P["st"])
     _lib.call("fk_moe_gemm_down", act.data_ptr(), R, H, P["w2"].data_ptr(), D, E,
-              plan.tile_expert.data_ptr(), plan.n_mblk.data_ptr(), y.data_ptr(), eptr, P["st"])
+              plan.tile_expert.data_ptr(), plan.n_mblk.data_ptr(), y.data_ptr(), 0, eptr,
+              P["st"])
     torch.cuda.synchronize()
     assert plan.err[1].item() == 0
     xf = xs[:rows].float()
@@ -167,13 +168,13 @@ def test_gemm_backward_pieces(n, k, E, D, H):
     st = P["st"]
     _lib.call("fk_moe_gemm_down_dgrad", dyb.data_ptr(), R, D, P["w2"].data_ptr(), H, E,
               plan.tile_expert.data_ptr(), plan.n_mblk.data_ptr(), h1b.data_ptr(), dh1.data_ptr(),
-              eptr, st)
+              0, eptr, st)
     _lib.call("fk_moe_gemm_up_dgrad", dh1.data_ptr(), R, H, P["w13"].data_ptr(), D, E,
-              plan.tile_expert.data_ptr(), plan.n_mblk.data_ptr(), dxs.data_ptr(), eptr, st)
+              plan.tile_expert.data_ptr(), plan.n_mblk.data_ptr(), dxs.data_ptr(), 0, eptr, st)
     _lib.call("fk_moe_gemm_wgrad", dyb.data_ptr(), D, actb.data_ptr(), H, R,
-              plan.seg_start.data_ptr(), E, dw2.data_ptr(), eptr, st)
+              plan.seg_start.data_ptr(), E, dw2.data_ptr(), 0, eptr, st)
     _lib.call("fk_moe_gemm_wgrad", dh1.data_ptr(), 2 * H, P["xs"].data_ptr(), D, R,
-              plan.seg_start.data_ptr(), E, dw13.data_ptr(), eptr, st)
+              plan.seg_start.data_ptr(), E, dw13.data_ptr(), 0, eptr, st)
     torch.cuda.synchronize()
     assert plan.err[1].item() == 0
     dact = torch.einsum("rd,rdh->rh", dy.float(), P["w2"].float()[eor])
@@ -193,6 +194,53 @@ def test_gemm_backward_pieces(n, k, E, D, H):
         else:
             close(dw2[e], ref2)
             close(dw13[e], ref13)
+
+
+@pytest.mark.parametrize("cap", [1, 7, 100])
+def test_gemm_grid_cap_is_bitwise_neutral(cap):
+    """max_ctas only changes which CTA computes a tile, never the tile's arithmetic: every
+    GEMM gives the same bits with the grid capped (the expert-parallel backward caps it to
+    leave SMs to a concurrent all-reduce)."""
+    n, k, E, D, H = 2048, 4, 16, 1024, 512
+    P = make_problem(n, k, E, D, H, seed=5)
+    plan, R = P["plan"], P["plan"].max_rows
+    te, nm, seg = plan.tile_expert.data_ptr(), plan.n_mblk.data_ptr(), plan.seg_start.data_ptr()
+    eptr = plan.err.data_ptr() + 4
+    st = P["st"]
+    bf = dict(dtype=torch.bfloat16, device=DEV)
+    G = gen(7)
+    dy = (torch.randn(R, D, generator=G) * 0.5).bfloat16().to(DEV)
+
+    def run(c):
+        h1 = torch.empty(R, 2 * H, **bf)
+        act = torch.empty(R, H, **bf)
+        y = torch.empty(R, D, **bf)
+        dh1 = torch.empty(R, 2 * H, **bf)
+        dxs = torch.empty(R, D, **bf)
+        dw2 = torch.empty(E, D, H, **bf)
+        dw13 = torch.empty(E, 2 * H, D, **bf)
+        _lib.call("fk_moe_gemm_up", P["xs"].data_ptr(), R, D, P["w13"].data_ptr(), H, E, te, nm,
+                  h1.data_ptr(), act.data_ptr(), c, eptr, st)
+        _lib.call("fk_moe_gemm_down", act.data_ptr(), R, H, P["w2"].data_ptr(), D, E, te, nm,
+                  y.data_ptr(), c, eptr, st)
+        _lib.call("fk_moe_gemm_down_dgrad", dy.data_ptr(), R, D, P["w2"].data_ptr(), H, E, te, nm,
+                  h1.data_ptr(), dh1.data_ptr(), c, eptr, st)
+        _lib.call("fk_moe_gemm_up_dgrad", dh1.data_ptr(), R, H, P["w13"].data_ptr(), D, E, te,
+                  nm, dxs.data_ptr(), c, eptr, st)
+        _lib.call("fk_moe_gemm_wgrad", dy.data_ptr(), D, act.data_ptr(), H, R, seg, E,
+                  dw2.data_ptr(), c, eptr, st)
+        _lib.call("fk_moe_gemm_wgrad", dh1.data_ptr(), 2 * H, P["xs"].data_ptr(), D, R, seg, E,
+                  dw13.data_ptr(), c, eptr, st)
+        torch.cuda.synchronize()
+        assert plan.err[1].item() == 0
+        rows = plan.n_mblk.item() * 128
+        return [t[:rows] for t in (h1, act, y, dh1, dxs)] + [dw2, dw13]
+
+    for a, b in zip(run(0), run(cap)):
+        assert torch.equal(a, b)
+    with pytest.raises(RuntimeError):
+        _lib.call("fk_moe_gemm_down", P["xs"].data_ptr(), R, H, P["w2"].data_ptr(), D, E, te,
+                  nm, P["xs"].data_ptr(), -1, eptr, st)
 
 
 def run_layer(layer, x, dout, bias=None):
