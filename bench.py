@@ -668,11 +668,13 @@ class MoELayer(Workload):
         self.ky = torch.empty(R, self.dim, **bf)
 
     def gemm_up(self):
+        """The up-projection of the layer step (SwiGLU and routing-weight epilogue)."""
         p = self.kp
-        self.lib.call("fk_moe_gemm_up", self.kxs.data_ptr(), p.max_rows, self.dim,
+        self.lib.call("fk_moe_gemm_up_weighted", self.kxs.data_ptr(), p.max_rows, self.dim,
                       self.layer.w13.data_ptr(), self.hidden, self.E, p.tile_expert.data_ptr(),
-                      p.n_mblk.data_ptr(), self.kh1.data_ptr(), self.kact.data_ptr(), 0,
-                      p.err.data_ptr() + 4, cur_stream())
+                      p.n_mblk.data_ptr(), p.sorted_assign.data_ptr(), p.sorted_w.data_ptr(),
+                      self.kh1.data_ptr(), self.kact.data_ptr(), 0, p.err.data_ptr() + 4,
+                      cur_stream())
 
     def gemm_down(self):
         p = self.kp
@@ -692,14 +694,15 @@ class MoELayer(Workload):
     @property
     def launches_per_step(self):
         """Kernels of this library per step.  One GPU: router fwd/bwd 2, metadata 2,
-        gather, up, down, combine | combine_bwd, 2 dgrad, 2 wgrad, combine = 14.
+        gather, up, down, combine | gather of dout, down dgrad, dw from parts, up dgrad,
+        2 wgrad, combine = 15.
         Expert parallel (peer transport): router 2, plan 2, 2 puts, 4 waits, metadata 2,
-        gather, up, down, 2 combine-puts, 2 unpack sums, unpack dw, combine_bwd, 2 dgrad,
-        2 wgrad (4 when experts are replicated) = 25 (27); NCCL transport: 2 packs and the
-        local combines instead of the puts, waits and combine-puts = 21 (23)."""
+        gather, up, down, 2 combine-puts, 2 unpack sums, unpack dw, gather of dout, dw from
+        parts, 2 dgrad, 2 wgrad (4 when experts are replicated) = 26 (28); NCCL transport:
+        2 packs and the local combines instead of the puts, waits and combine-puts = 22 (24)."""
         if self.world == 1:
-            return 14
-        base = 25 if self.ep_transport == "peer" else 21
+            return 15
+        base = 26 if self.ep_transport == "peer" else 22
         return base + (2 if self.replicated else 0)
 
     def units_per_step(self):

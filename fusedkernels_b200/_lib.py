@@ -46,6 +46,11 @@ SIGNATURES: dict[str, list] = {
                                _vp],
     "fk_moe_gemm_up_dgrad": [_vp, _i64, _i32, _vp, _i32, _i32, _vp, _vp, _vp, _i32, _vp, _vp],
     "fk_moe_gemm_wgrad": [_vp, _i32, _vp, _i32, _i64, _vp, _i32, _vp, _i32, _vp, _vp],
+    "fk_moe_gemm_up_weighted": [_vp, _i64, _i32, _vp, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp,
+                                _i32, _vp, _vp],
+    "fk_moe_gemm_down_dgrad_weighted": [_vp, _i64, _i32, _vp, _i32, _i32, _vp, _vp, _vp, _vp,
+                                        _vp, _vp, _vp, _i32, _vp, _vp],
+    "fk_moe_dw_from_parts": [_vp, _i32, _vp, _vp, _i64, _vp, _vp],
     "fk_tf32_split": [_vp, _i64, _vp, _vp, _vp],
     "fk_moe_gemm_up_typed": [_vp, _vp, _i64, _i32, _vp, _vp, _i32, _i32, _vp, _vp, _vp, _vp,
                              _i32, _vp, _vp],

@@ -102,6 +102,11 @@ struct Params {
   int64_t ldi0;
   int* err;
   int tma_store;  // epilogue writes through shared memory + TMA stores (tmC0 / tmC1)
+  // Row-weighted epilogues (ROWW): row_assign[r] < 0 marks a padding row, row_w[r] is the
+  // routing weight of sorted row r; dw_part receives the routing-weight partial dots.
+  const int* row_assign;
+  const float* row_w;
+  float* dw_part;  // EPI_SWIGLU_BWD with ROWW: [rows, H / 64] fp32
 };
 
 __device__ __forceinline__ uint64_t globaltimer() {
@@ -351,7 +356,10 @@ __device__ __forceinline__ Tile decode(const Params& p, int t, const uint8_t* or
 }
 
 // tmA/tmB: operands (KIND_TF32X3: their hi parts); tmA2/tmB2: the lo parts (TF32X3 only).
-template <int BN, int STAGES, bool A_MN, bool B_MN, int MODE, int EPI, int KIND>
+// ROWW (MODE_M SwiGLU epilogues): the routing weight of each row is applied in the
+// epilogue (forward: out0 = w * silu(g) * u; backward: d(act) = w * accumulator, plus the
+// routing-weight gradient partials), and padding rows come out as exact zeros.
+template <int BN, int STAGES, bool A_MN, bool B_MN, int MODE, int EPI, int KIND, bool ROWW = false>
 __global__ void __launch_bounds__(kThreads, 1)
     moe_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
                     const __grid_constant__ CUtensorMap tmB,
@@ -363,6 +371,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   using T = typename KT::T;
   constexpr int BKE = KT::kBKE;
   constexpr int PASSES = KT::kPasses;
+  static_assert(!ROWW || (MODE == MODE_M && EPI != EPI_STORE), "row weights: SwiGLU epilogues");
   constexpr bool kRing = sizeof(T) == 2;  // TMA-store ring for 16-bit outputs
   constexpr uint32_t A_BYTES = BM * 128;
   constexpr uint32_t B_BYTES = BN * 128;
@@ -555,6 +564,14 @@ __global__ void __launch_bounds__(kThreads, 1)
             else store32(dst + c, v);
           }
         } else if (EPI == EPI_SWIGLU_FWD) {
+          // ROWW: out0 is the routing-weighted activation w[row] * silu(g) * u (zero on
+          // padding rows), so the down-projection yields weighted rows.
+          bool vrow = true;
+          float rw = 1.0f;
+          if constexpr (ROWW) {
+            vrow = p.row_assign[row] >= 0;
+            rw = vrow ? p.row_w[row] : 0.0f;
+          }
           T* act = static_cast<T*>(p.out0) + row * p.ld0 + tl.n0;
           T* hg = static_cast<T*>(p.out1) + row * p.ld1 + tl.n0;
           T* hu = static_cast<T*>(p.out1) + row * p.ld1 + p.H + tl.n0;
@@ -564,7 +581,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             tmem_ld32(tbase + c, g);
             tmem_ld32(tbase + BN / 2 + c, u);
 #pragma unroll
-            for (int i = 0; i < 32; ++i) a[i] = g[i] * sigmoidf_t<T>(g[i]) * u[i];
+            for (int i = 0; i < 32; ++i) {
+              a[i] = g[i] * sigmoidf_t<T>(g[i]) * u[i];
+              if constexpr (ROWW) a[i] = vrow ? rw * a[i] : 0.0f;
+            }
             if (tma_out) {
               ring.put(&tmC1, tl.n0 + c, row0, g, lane);
               ring.put(&tmC1, p.H + tl.n0 + c, row0, u, lane);
@@ -576,6 +596,17 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           }
         } else {  // EPI_SWIGLU_BWD: accumulator = d(act) for hidden units n0 .. n0+BN
+          // ROWW: A holds the unweighted output-gradient rows, so the accumulator is
+          // dout[token] @ w2.  d(act) is w[row] times it, and the routing-weight gradient of
+          // the row, <dout[token], y_row> = <dout[token] @ w2, act_row>, is summed here over
+          // this tile's hidden units into dw_part (act recomputed from g, u).  Padding rows
+          // give zeros.
+          bool vrow = true;
+          float rw = 1.0f, dot = 0.0f;
+          if constexpr (ROWW) {
+            vrow = p.row_assign[row] >= 0;
+            rw = vrow ? p.row_w[row] : 0.0f;
+          }
           const T* hg = static_cast<const T*>(p.in0) + row * p.ldi0 + tl.n0;
           const T* hu = static_cast<const T*>(p.in0) + row * p.ldi0 + p.H + tl.n0;
           T* dg = static_cast<T*>(p.out0) + row * p.ld0 + tl.n0;
@@ -589,8 +620,17 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
             for (int i = 0; i < 32; ++i) {
               const float sg = sigmoidf_t<T>(g[i]);
-              ou[i] = d[i] * g[i] * sg;
-              og[i] = d[i] * u[i] * (sg * (1.0f + g[i] * (1.0f - sg)));
+              float dd = d[i];
+              if constexpr (ROWW) {
+                dot = fmaf(d[i], g[i] * sg * u[i], dot);
+                dd = rw * d[i];
+              }
+              ou[i] = dd * g[i] * sg;
+              og[i] = dd * u[i] * (sg * (1.0f + g[i] * (1.0f - sg)));
+              if constexpr (ROWW) {
+                ou[i] = vrow ? ou[i] : 0.0f;
+                og[i] = vrow ? og[i] : 0.0f;
+              }
             }
             if (tma_out) {
               ring.put(&tmC0, tl.n0 + c, row0, og, lane);
@@ -599,6 +639,14 @@ __global__ void __launch_bounds__(kThreads, 1)
               store32(dg + c, og);
               store32(du + c, ou);
             }
+          }
+          if constexpr (ROWW) {
+            // one slot per 64 hidden units: this tile's dot in its first slot, zeros in the
+            // rest, so the layout does not depend on the tile width
+            float* dp = p.dw_part + row * (p.H / 64) + tl.n0 / 64;
+            dp[0] = vrow ? dot : 0.0f;
+#pragma unroll
+            for (int j = 1; j < BN / 64; ++j) dp[j] = 0.0f;
           }
         }
       }
@@ -661,7 +709,7 @@ constexpr CUtensorMapSwizzle mn_swizzle() {
   return KIND == KIND_TF32X3 ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B;
 }
 
-template <int BN, bool A_MN, bool B_MN, int MODE, int EPI, int KIND>
+template <int BN, bool A_MN, bool B_MN, int MODE, int EPI, int KIND, bool ROWW = false>
 int launch(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& c0,
            const CUtensorMap& c1, const CUtensorMap& a2, const CUtensorMap& b2, const Params& p,
            int max_tiles, cudaStream_t st, int max_ctas) {
@@ -669,7 +717,7 @@ int launch(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& c0,
   constexpr int STAGE_BYTES = (BM + BN) * 128;
   constexpr int STAGES = (BN == 256) ? 4 : (BN == 128 ? 6 : 8);
   constexpr int SMEM = STAGES * STAGE_BYTES + (kRing ? 4 * (int)kRingBytesPerWarp : 0) + 1024 + 256;
-  auto k = moe_gemm_kernel<BN, STAGES, A_MN, B_MN, MODE, EPI, KIND>;
+  auto k = moe_gemm_kernel<BN, STAGES, A_MN, B_MN, MODE, EPI, KIND, ROWW>;
   cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
   int grid = num_sms();
   if (max_ctas > 0 && max_ctas < grid) grid = max_ctas;  // SMs left to concurrent work

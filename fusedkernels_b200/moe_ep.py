@@ -279,28 +279,31 @@ class _EPMoEFn(torch.autograd.Function):
         y = torch.empty(R, d, **bf)
         _lib.call("fk_moe_gather", recv_x_p, d, plan.sorted_assign.data_ptr(), k,
                   plan.n_mblk.data_ptr(), R, xs.data_ptr(), _lib.FK_BF16, st)
-        _lib.call("fk_moe_gemm_up", xs.data_ptr(), R, d, layer.w13.data_ptr(), H, El,
-                  plan.tile_expert.data_ptr(), plan.n_mblk.data_ptr(), h1.data_ptr(),
+        # routing weights applied in the up-projection's epilogue (act = w * silu(g) * u):
+        # the expert rows come out weighted and the local slots are summed unweighted
+        _lib.call("fk_moe_gemm_up_weighted", xs.data_ptr(), R, d, layer.w13.data_ptr(), H, El,
+                  plan.tile_expert.data_ptr(), plan.n_mblk.data_ptr(),
+                  plan.sorted_assign.data_ptr(), plan.sorted_w.data_ptr(), h1.data_ptr(),
                   act.data_ptr(), 0, eptr + 4, st)
         _lib.call("fk_moe_gemm_down", act.data_ptr(), R, H, layer.w2.data_ptr(), d, El,
                   plan.tile_expert.data_ptr(), plan.n_mblk.data_ptr(), y.data_ptr(), 0, eptr + 4,
                   st)
         if px is not None:
-            _lib.call("fk_ep_peer_combine_put", y.data_ptr(), d, plan.slot_pos.data_ptr(), recv_w_p,
+            _lib.call("fk_ep_peer_combine_put", y.data_ptr(), d, plan.slot_pos.data_ptr(), None,
                       T, N, ex.rank, k, None, px.table("to_source"), None, px.table("flags"),
                       px.PHASE_FWD_COMBINE, px.ctl.data_ptr(), _lib.FK_BF16, st)
             px.wait(px.PHASE_FWD_COMBINE, st)
             back_p = px.local("to_source")
         else:
             partial = torch.empty(R_tok, d, **bf)
-            _lib.call("fk_moe_combine", y.data_ptr(), d, plan.slot_pos.data_ptr(), recv_w_p,
+            _lib.call("fk_moe_combine", y.data_ptr(), d, plan.slot_pos.data_ptr(), None,
                       R_tok, k, partial.data_ptr(), _lib.FK_BF16, st)
             back = ex.all_to_all(partial)
             back_p = back.data_ptr()
         out = torch.empty(T, d, **bf)
         _lib.call("fk_ep_unpack_sum", back_p, d, src_pos.data_ptr(), T, N, out.data_ptr(),
                   _lib.FK_BF16, st)
-        ctx.save_for_backward(xs, h1, act, y, idx, src_pos, send_token)
+        ctx.save_for_backward(xs, h1, act, idx, src_pos, send_token)
         ctx.plan = plan
         ctx.layer = layer
         ctx.dims = (T, d, k, N, El, H, E)
@@ -308,7 +311,7 @@ class _EPMoEFn(torch.autograd.Function):
 
     @staticmethod
     def backward(ctx, dout):
-        xs, h1, act, y, idx, src_pos, send_token = ctx.saved_tensors
+        xs, h1, act, idx, src_pos, send_token = ctx.saved_tensors
         plan, layer = ctx.plan, ctx.layer
         T, d, k, N, El, H, E = ctx.dims
         ex = layer.exchange
@@ -341,9 +344,11 @@ class _EPMoEFn(torch.autograd.Function):
         dw2 = torch.empty(El, d, H, **bf)
         te, nm = plan.tile_expert.data_ptr(), plan.n_mblk.data_ptr()
         seg = plan.seg_start.data_ptr()
-        _lib.call("fk_moe_combine_bwd", recv_d_p, y.data_ptr(), d,
-                  plan.sorted_assign.data_ptr(), plan.sorted_w.data_ptr(), k,
-                  plan.n_mblk.data_ptr(), R, dy.data_ptr(), dw_recv.data_ptr(), _lib.FK_BF16, st)
+        # dy: the received output-gradient rows, unweighted; the down-projection's input
+        # gradient applies the routing weight and forms the routing-weight gradient
+        sa, sw = plan.sorted_assign.data_ptr(), plan.sorted_w.data_ptr()
+        _lib.call("fk_moe_gather", recv_d_p, d, sa, k, nm, R, dy.data_ptr(), _lib.FK_BF16, st)
+        part = torch.empty(R, H // 64, dtype=torch.float32, device=dev)
 
         def wgrad(lo, hi, cap, which):
             """Weight gradients of stacked experts lo..hi-1 (dW2 or dW13)."""
@@ -367,8 +372,10 @@ class _EPMoEFn(torch.autograd.Function):
         if rep:
             wgrad(n_own, El, 0, 2)
             red.append(dist.all_reduce(dw2[n_own:], group=ex.group, async_op=True))
-        _lib.call("fk_moe_gemm_down_dgrad", dy.data_ptr(), R, d, layer.w2.data_ptr(), H, El,
-                  te, nm, h1.data_ptr(), dh1.data_ptr(), cap, eptr + 4, st)
+        _lib.call("fk_moe_gemm_down_dgrad_weighted", dy.data_ptr(), R, d, layer.w2.data_ptr(),
+                  H, El, te, nm, sa, sw, h1.data_ptr(), dh1.data_ptr(), part.data_ptr(), cap,
+                  eptr + 4, st)
+        _lib.call("fk_moe_dw_from_parts", part.data_ptr(), H, sa, nm, R, dw_recv.data_ptr(), st)
         if rep:
             wgrad(n_own, El, cap, 13)
             red.append(dist.all_reduce(dw13[n_own:], group=ex.group, async_op=True))

@@ -6,14 +6,17 @@ ModuleList of ``Expert``), same state_dict keys and the same forward semantics
 (out[t] = sum_j w[t,j] * Expert_{idx[t,j]}(x[t])).  The body differs:
 
   router GEMM (nn.Linear) -> fused_moe_route_v2 -> fk_moe_route_meta (stable counting sort,
-  128-row padded expert segments, all on the device) -> fk_moe_gather -> fk_moe_gemm_up
-  (tcgen05 grouped GEMM, SwiGLU epilogue) -> fk_moe_gemm_down -> fk_moe_combine
-  (per-token fp32 sum in slot order: deterministic, no index_add_ atomics).
+  128-row padded expert segments, all on the device) -> fk_moe_gather -> fk_moe_gemm_up_weighted
+  (tcgen05 grouped GEMM, SwiGLU and routing-weight epilogue) -> fk_moe_gemm_down ->
+  fk_moe_combine (per-token fp32 sum in slot order: deterministic, no index_add_ atomics).
 
 There is no device->host synchronisation (the reference reads the expert counts back with
 .tolist(), moe_layer_sorted.py:67-68): every buffer is sized for the worst case
-N*k + E*127 rows.  Backward runs fk_moe_combine_bwd, the dgrad GEMMs with the SwiGLU
-backward fused into the epilogue, and the per-expert weight-gradient GEMMs.
+N*k + E*127 rows.  Backward gathers dout's rows, runs the input-gradient GEMMs (the
+down-projection's fuses the SwiGLU backward, the routing weight and the routing-weight
+gradient into its epilogue) and the per-expert weight-gradient GEMMs.  fp16 and fp32
+layers apply the routing weight in the combine kernels instead (fk_moe_combine_bwd in
+backward).
 
 Expert weights live in two stacked buffers, w13 [E, 2H, D] (gate rows then up rows) and
 w2 [E, D, H]; every ``experts[e].w_*.weight`` Parameter is a view into them (re-pointed at
@@ -97,6 +100,34 @@ class _SortedMoEFn(torch.autograd.Function):
                   plan.n_mblk.data_ptr(), plan.sorted_assign.data_ptr(), plan.sorted_w.data_ptr(),
                   plan.slot_pos.data_ptr(), R, plan.ws.data_ptr(), plan.ws.numel(), eptr, st)
         td = dict(dtype=dt, device=dev)
+        ctx.plan = plan
+        ctx.layer = layer
+        ctx.dims = (n, d, k, E, H)
+        ctx.weighted = dt == torch.bfloat16
+        if ctx.weighted:
+            # The routing weight is applied in the up-projection's epilogue (act_w =
+            # w * silu(g) * u), so the down-projection gives weighted rows that the combine
+            # sums unweighted; the backward then needs no pass over the output rows.
+            xs = torch.empty(R, d, **td)
+            h1 = torch.empty(R, 2 * H, **td)
+            act_w = torch.empty(R, H, **td)
+            y = torch.empty(R, d, **td)
+            out = torch.empty(n, d, **td)
+            if R > 0:
+                te, nm = plan.tile_expert.data_ptr(), plan.n_mblk.data_ptr()
+                _lib.call("fk_moe_gather", x.data_ptr(), d, plan.sorted_assign.data_ptr(), k,
+                          nm, R, xs.data_ptr(), code, st)
+                _lib.call("fk_moe_gemm_up_weighted", xs.data_ptr(), R, d, layer.w13.data_ptr(),
+                          H, E, te, nm, plan.sorted_assign.data_ptr(), plan.sorted_w.data_ptr(),
+                          h1.data_ptr(), act_w.data_ptr(), 0, eptr + 4, st)
+                _lib.call("fk_moe_gemm_down", act_w.data_ptr(), R, H, layer.w2.data_ptr(), d, E,
+                          te, nm, y.data_ptr(), 0, eptr + 4, st)
+            _lib.call("fk_moe_combine", y.data_ptr(), d, plan.slot_pos.data_ptr(), None, n, k,
+                      out.data_ptr(), code, st)
+            if layer.check_errors:
+                _check_err(plan)
+            ctx.save_for_backward(xs, h1, act_w)
+            return out
         xs = torch.empty(R, d, **td)
         h1 = torch.empty(R, 2 * H, **td)
         act = torch.empty(R, H, **td)
@@ -129,13 +160,12 @@ class _SortedMoEFn(torch.autograd.Function):
             _check_err(plan)
         # fp32: xs / act are the hi parts and xs_lo / act_lo the lo parts
         ctx.save_for_backward(xs, h1, act, y, xs_lo, act_lo)
-        ctx.plan = plan
-        ctx.layer = layer
-        ctx.dims = (n, d, k, E, H)
         return out
 
     @staticmethod
     def backward(ctx, dout):
+        if ctx.weighted:
+            return _SortedMoEFn._backward_weighted(ctx, dout)
         xs, h1, act, y, xs_lo, act_lo = ctx.saved_tensors
         plan, layer = ctx.plan, ctx.layer
         n, d, k, E, H = ctx.dims
@@ -186,6 +216,60 @@ class _SortedMoEFn(torch.autograd.Function):
                 _lib.call("fk_moe_gemm_wgrad_typed", dh1.data_ptr(), _p(dh1_lo), 2 * H,
                           xs.data_ptr(), _p(xs_lo), d, R, seg, E, dw13.data_ptr(), code,
                           eptr + 4, st)
+            _lib.call("fk_moe_combine", dxs.data_ptr(), d, plan.slot_pos.data_ptr(), None, n, k,
+                      dx.data_ptr(), code, st)
+        else:
+            dw.zero_()
+            dw13.zero_()
+            dw2.zero_()
+            dx.zero_()
+        if layer.check_errors:
+            _check_err(plan)
+        grads = []
+        for e in range(E):
+            grads += [dw13[e, :H], dw13[e, H:], dw2[e]]
+        return (dx, dw, None, None, *grads)
+
+
+    @staticmethod
+    def _backward_weighted(ctx, dout):
+        """Backward of the row-weighted bf16 path: dout's rows are gathered unweighted; the
+        down-projection's input-gradient epilogue applies the routing weight and forms the
+        routing-weight gradient partials (fk_moe_dw_from_parts sums them)."""
+        xs, h1, act_w = ctx.saved_tensors
+        plan, layer = ctx.plan, ctx.layer
+        n, d, k, E, H = ctx.dims
+        R = plan.max_rows
+        dev, dt = xs.device, xs.dtype
+        code = _lib.dtype_code(dt)
+        st = _lib.stream_of(xs)
+        eptr = plan.err.data_ptr()
+        dout = dout.to(dt).contiguous()
+        td = dict(dtype=dt, device=dev)
+        dw = torch.empty(n, k, dtype=torch.float32, device=dev)
+        dw13 = torch.empty(E, 2 * H, d, **td)
+        dw2 = torch.empty(E, d, H, **td)
+        dx = torch.empty(n, d, **td)
+        if R > 0:
+            te, nm, seg = plan.tile_expert.data_ptr(), plan.n_mblk.data_ptr(), plan.seg_start.data_ptr()
+            sa, sw = plan.sorted_assign.data_ptr(), plan.sorted_w.data_ptr()
+            dy = torch.empty(R, d, **td)
+            _lib.call("fk_moe_gather", dout.data_ptr(), d, sa, k, nm, R, dy.data_ptr(), code, st)
+            dh1 = torch.empty(R, 2 * H, **td)
+            part = torch.empty(R, H // 64, dtype=torch.float32, device=dev)
+            _lib.call("fk_moe_gemm_down_dgrad_weighted", dy.data_ptr(), R, d, layer.w2.data_ptr(),
+                      H, E, te, nm, sa, sw, h1.data_ptr(), dh1.data_ptr(), part.data_ptr(), 0,
+                      eptr + 4, st)
+            _lib.call("fk_moe_dw_from_parts", part.data_ptr(), H, sa, nm, R, dw.data_ptr(), st)
+            _lib.call("fk_moe_gemm_wgrad", dy.data_ptr(), d, act_w.data_ptr(), H, R, seg, E,
+                      dw2.data_ptr(), 0, eptr + 4, st)
+            del dy
+            dxs = torch.empty(R, d, **td)
+            _lib.call("fk_moe_gemm_up_dgrad", dh1.data_ptr(), R, H, layer.w13.data_ptr(), d, E,
+                      te, nm, dxs.data_ptr(), 0, eptr + 4, st)
+            _lib.call("fk_moe_gemm_wgrad", dh1.data_ptr(), 2 * H, xs.data_ptr(), d, R, seg, E,
+                      dw13.data_ptr(), 0, eptr + 4, st)
+            del dh1
             _lib.call("fk_moe_combine", dxs.data_ptr(), d, plan.slot_pos.data_ptr(), None, n, k,
                       dx.data_ptr(), code, st)
         else:

@@ -223,6 +223,36 @@ FK_API int fk_moe_gemm_wgrad(const void* a, int m_dim, const void* b, int n_dim,
                              int64_t max_rows, const int* seg_start, int n_experts, void* dw,
                              int max_ctas, int* err_flag, void* stream);
 
+/* Row-weighted variants (bf16): the routing weight of every sorted row is applied in the
+ * SwiGLU epilogues instead of by the combine kernels, and padding rows come out as zeros.
+ * fk_moe_gemm_up_weighted: h1 = xs @ w13[e]^T, act_w = sorted_w[r] * silu(g) * u;
+ *                         fk_moe_gemm_down on act_w then gives weighted rows, which
+ *                         fk_moe_combine sums unweighted (w = NULL).
+ * fk_moe_gemm_down_dgrad_weighted: dy holds the UNWEIGHTED output-gradient rows
+ *                         (fk_moe_gather of dout); dh1 = SwiGLU'(sorted_w[r] * (dy @ w2[e]),
+ *                         h1), and dw_part [max_rows, hidden / 64] fp32 receives, per 64
+ *                         hidden units, the partial dots of <dy @ w2[e], act> (act
+ *                         recomputed from h1).
+ * fk_moe_dw_from_parts:   dw[sorted_assign[r]] = sum of row r's partials (fixed order) =
+ *                         <dout[token], y_r> with y_r the row's unweighted expert output:
+ *                         the routing-weight gradient fk_moe_combine_bwd computes.
+ * With fk_moe_gemm_wgrad(dy, act_w) for dW2 (= sum of (w dout)^T act) they replace
+ * fk_moe_combine_bwd in the layer's bf16 backward (moe_layer_sorted.py:70-85): a row gather
+ * of dout instead of a pass that also re-reads every output row. */
+FK_API int fk_moe_gemm_up_weighted(const void* xs, int64_t max_rows, int dim, const void* w13,
+                                   int hidden, int n_experts, const int* tile_expert,
+                                   const int* n_mblk, const int* sorted_assign,
+                                   const float* sorted_w, void* h1, void* act_w, int max_ctas,
+                                   int* err_flag, void* stream);
+FK_API int fk_moe_gemm_down_dgrad_weighted(const void* dy, int64_t max_rows, int dim,
+                                           const void* w2, int hidden, int n_experts,
+                                           const int* tile_expert, const int* n_mblk,
+                                           const int* sorted_assign, const float* sorted_w,
+                                           const void* h1, void* dh1, float* dw_part,
+                                           int max_ctas, int* err_flag, void* stream);
+FK_API int fk_moe_dw_from_parts(const float* dw_part, int hidden, const int* sorted_assign,
+                                const int* n_mblk, int64_t max_rows, float* dw, void* stream);
+
 /* Typed variants for fp16 and fp32 layers (the reference's layers run in the caller's dtype,
  * fp32 by default: moe_layer_sorted.py:28-37, moe_layer.py:22-31).  dtype: FK_BF16 (same as
  * the entry points above), FK_F16 (fp16 operands and outputs, kind::f16 MMAs) or FK_F32.

@@ -196,6 +196,64 @@ def test_gemm_backward_pieces(n, k, E, D, H):
             close(dw13[e], ref13)
 
 
+@pytest.mark.parametrize("n,k,E,D,H", SHAPES)
+def test_row_weighted_epilogues(n, k, E, D, H):
+    """The row-weighted GEMM variants against the plain ones and PyTorch fp32: h1
+    bit-identical (same operands), act_w = w * act, zero padding rows; the weighted
+    input-gradient GEMM on unweighted dout rows gives SwiGLU'(w * dy @ w2) and the
+    routing-weight gradient <dout[token], y_row> through fk_moe_dw_from_parts."""
+    P = make_problem(n, k, E, D, H, seed=3 * n + D)
+    plan, R, st = P["plan"], P["plan"].max_rows, P["st"]
+    te, nm = plan.tile_expert.data_ptr(), plan.n_mblk.data_ptr()
+    sa, sw = plan.sorted_assign, plan.sorted_w
+    eptr = plan.err.data_ptr() + 4
+    eor, rows = expert_of_rows(plan)
+    bf = dict(dtype=torch.bfloat16, device=DEV)
+    h1, act = torch.empty(R, 2 * H, **bf), torch.empty(R, H, **bf)
+    _lib.call("fk_moe_gemm_up", P["xs"].data_ptr(), R, D, P["w13"].data_ptr(), H, E, te, nm,
+              h1.data_ptr(), act.data_ptr(), 0, eptr, st)
+    h1w, actw = torch.full((R, 2 * H), 7.0, **bf), torch.full((R, H), 7.0, **bf)
+    _lib.call("fk_moe_gemm_up_weighted", P["xs"].data_ptr(), R, D, P["w13"].data_ptr(), H, E, te,
+              nm, sa.data_ptr(), sw.data_ptr(), h1w.data_ptr(), actw.data_ptr(), 0, eptr, st)
+    torch.cuda.synchronize()
+    assert plan.err[1].item() == 0
+    valid = (sa[:rows] >= 0)
+    assert torch.equal(h1w[:rows], h1[:rows])
+    wrow = torch.where(valid, sw[:rows], 0.0)[:, None]
+    close(actw[:rows], act[:rows].float() * wrow)
+    assert torch.count_nonzero(actw[:rows][~valid]) == 0
+
+    G = gen(11)
+    dout = torch.randn(n, D, generator=G).bfloat16().to(DEV)
+    dy = torch.empty(R, D, **bf)
+    _lib.call("fk_moe_gather", dout.data_ptr(), D, sa.data_ptr(), k, nm, R, dy.data_ptr(),
+              _lib.FK_BF16, st)
+    dh1 = torch.full((R, 2 * H), 7.0, **bf)
+    part = torch.full((R, H // 64), 7.0, dtype=torch.float32, device=DEV)
+    _lib.call("fk_moe_gemm_down_dgrad_weighted", dy.data_ptr(), R, D, P["w2"].data_ptr(), H, E,
+              te, nm, sa.data_ptr(), sw.data_ptr(), h1w.data_ptr(), dh1.data_ptr(),
+              part.data_ptr(), 0, eptr, st)
+    dw = torch.full((n * k,), 7.0, dtype=torch.float32, device=DEV)
+    _lib.call("fk_moe_dw_from_parts", part.data_ptr(), H, sa.data_ptr(), nm, R, dw.data_ptr(), st)
+    torch.cuda.synchronize()
+    assert plan.err[1].item() == 0
+    tok = torch.where(valid, sa[:rows] // k, 0).long()
+    g, u = h1w[:rows, :H].float(), h1w[:rows, H:].float()
+    dsum = torch.einsum("rd,rdh->rh", dout[tok].float(), P["w2"].float()[eor])
+    dact = dsum * wrow
+    sg = torch.sigmoid(g)
+    ref_dh1 = torch.cat([dact * u * sg * (1 + g * (1 - sg)), dact * g * sg], dim=1)
+    close(dh1[:rows], torch.where(valid[:, None], ref_dh1, 0.0))
+    assert torch.count_nonzero(dh1[:rows][~valid]) == 0
+    ref_dw_rows = (dsum * (F.silu(g) * u)).sum(1)
+    ref_dw = torch.zeros(n * k, device=DEV)
+    ref_dw[sa[:rows][valid].long()] = ref_dw_rows[valid]
+    close(dw, ref_dw)
+    with pytest.raises(RuntimeError):
+        _lib.call("fk_moe_gemm_up_weighted", P["xs"].data_ptr(), R, D, P["w13"].data_ptr(), H, E,
+                  te, nm, None, sw.data_ptr(), h1w.data_ptr(), actw.data_ptr(), 0, eptr, st)
+
+
 @pytest.mark.parametrize("cap", [1, 7, 100])
 def test_gemm_grid_cap_is_bitwise_neutral(cap):
     """max_ctas only changes which CTA computes a tile, never the tile's arithmetic: every
