@@ -308,13 +308,13 @@ struct Tile {
   bool valid;
 };
 
-template <int BN, int MODE, int EPI>
+template <int BN, int MODE, int EPI, int MB>
 __device__ __forceinline__ int num_tiles(const Params& p) {
   if (MODE == MODE_M) {
     const int nnb = (EPI == EPI_SWIGLU_FWD) ? p.H / (BN / 2) : p.N / BN;
     return (*p.n_mblk) * nnb;
   }
-  const int nmb = (p.M + BM - 1) / BM, nnb = p.N / BN;
+  const int nmb = (p.M + BM * MB - 1) / (BM * MB), nnb = p.N / BN;
   return p.E * nmb * nnb;
 }
 
@@ -322,8 +322,9 @@ __device__ __forceinline__ int num_tiles(const Params& p) {
 // the tiles out in a serpentine over the CTAs (pass i goes left to right when i is even,
 // right to left when odd), so the tiles of the few hot experts of a skewed routing spread
 // evenly over the SMs instead of piling up on the CTAs their position happens to hit.
-// t runs over whole passes; tiles past the end are invalid.  BKE = elements of K per stage.
-template <int BN, int MODE, int EPI, int BKE>
+// t runs over whole passes; tiles past the end are invalid.  BKE = elements of K per stage;
+// MB = 128-row blocks of M per tile (MODE_K).
+template <int BN, int MODE, int EPI, int BKE, int MB>
 __device__ __forceinline__ Tile decode(const Params& p, int t, const uint8_t* order, int ntiles) {
   Tile tl;
   tl.valid = true;
@@ -337,7 +338,7 @@ __device__ __forceinline__ Tile decode(const Params& p, int t, const uint8_t* or
     tl.kb0 = 0;
     tl.kiters = p.K / BKE;
   } else {
-    const int nmb = (p.M + BM - 1) / BM, nnb = p.N / BN;
+    const int nmb = (p.M + BM * MB - 1) / (BM * MB), nnb = p.N / BN;
     const int G = gridDim.x, pass = t / G, j = t % G;
     const int g = pass * G + ((pass & 1) ? G - 1 - j : j);
     if (g >= ntiles) {
@@ -346,7 +347,7 @@ __device__ __forceinline__ Tile decode(const Params& p, int t, const uint8_t* or
     }
     tl.e = order[g / (nmb * nnb)];
     const int r = g % (nmb * nnb);
-    tl.m0 = (r / nnb) * BM;
+    tl.m0 = (r / nnb) * BM * MB;
     tl.n0 = (r % nnb) * BN;
     const int s0 = p.seg_start[tl.e], s1 = p.seg_start[tl.e + 1];
     tl.kb0 = s0 / BKE;
@@ -359,7 +360,12 @@ __device__ __forceinline__ Tile decode(const Params& p, int t, const uint8_t* or
 // ROWW (MODE_M SwiGLU epilogues): the routing weight of each row is applied in the
 // epilogue (forward: out0 = w * silu(g) * u; backward: d(act) = w * accumulator, plus the
 // routing-weight gradient partials), and padding rows come out as exact zeros.
-template <int BN, int STAGES, bool A_MN, bool B_MN, int MODE, int EPI, int KIND, bool ROWW = false>
+// MB = 2 (MODE_K, 16-bit): a tile is 256 x BN, two accumulators side by side in TMEM fed by
+// one B stage (a tile of a weight gradient with more tiles per expert than SMs would
+// otherwise run in several waves, each re-reading the expert's operands from HBM); the
+// accumulators are then single-buffered.
+template <int BN, int STAGES, bool A_MN, bool B_MN, int MODE, int EPI, int KIND, bool ROWW = false,
+          int MB = 1>
 __global__ void __launch_bounds__(kThreads, 1)
     moe_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
                     const __grid_constant__ CUtensorMap tmB,
@@ -372,12 +378,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr int BKE = KT::kBKE;
   constexpr int PASSES = KT::kPasses;
   static_assert(!ROWW || (MODE == MODE_M && EPI != EPI_STORE), "row weights: SwiGLU epilogues");
+  static_assert(MB == 1 || (MB == 2 && MODE == MODE_K && KIND != KIND_TF32X3),
+                "256-row tiles: 16-bit weight gradients");
+  constexpr int NBUF = MB == 1 ? 2 : 1;  // accumulator sets in TMEM (double-buffered if 2)
   constexpr bool kRing = sizeof(T) == 2;  // TMA-store ring for 16-bit outputs
-  constexpr uint32_t A_BYTES = BM * 128;
+  constexpr uint32_t A_BYTES = MB * BM * 128;
   constexpr uint32_t B_BYTES = BN * 128;
   constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
   constexpr uint32_t BOX_BYTES = BKE * 128;  // one BKE x BKE MN-major box
-  constexpr uint32_t TMEM_COLS = 2 * BN;
+  constexpr uint32_t TMEM_COLS = NBUF * MB * BN;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem = reinterpret_cast<unsigned char*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -424,7 +433,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-  const int ntiles = num_tiles<BN, MODE, EPI>(p);
+  const int ntiles = num_tiles<BN, MODE, EPI, MB>(p);
   const int tiles_loop =
       MODE == MODE_K ? (ntiles + (int)gridDim.x - 1) / (int)gridDim.x * (int)gridDim.x : ntiles;
 
@@ -435,7 +444,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t ph = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < tiles_loop && ok; t += gridDim.x) {
-        const Tile tl = decode<BN, MODE, EPI, BKE>(p, t, order, ntiles);
+        const Tile tl = decode<BN, MODE, EPI, BKE, MB>(p, t, order, ntiles);
         if (!tl.valid) continue;
         const int total = tl.kiters * PASSES;
         for (int it = 0; it < total; ++it) {
@@ -452,7 +461,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             tma2d(sa, ma, k0, tl.m0, &full[s]);
           } else {
 #pragma unroll
-            for (int i = 0; i < BM / BKE; ++i) tma2d(sa + i * BOX_BYTES, ma, tl.m0 + BKE * i, k0, &full[s]);
+            for (int i = 0; i < MB * BM / BKE; ++i) tma2d(sa + i * BOX_BYTES, ma, tl.m0 + BKE * i, k0, &full[s]);
           }
           if (EPI == EPI_SWIGLU_FWD) {
             tma3d(sb, mb, k0, tl.n0, tl.e, &full[s]);
@@ -486,14 +495,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       int it = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < tiles_loop && ok; t += gridDim.x) {
-        const Tile tl = decode<BN, MODE, EPI, BKE>(p, t, order, ntiles);
+        const Tile tl = decode<BN, MODE, EPI, BKE, MB>(p, t, order, ntiles);
         if (!tl.valid) continue;
-        const int acc = it & 1;
-        const uint32_t aph = (uint32_t)((it >> 1) & 1);
+        const int acc = NBUF == 2 ? (it & 1) : 0;
+        const uint32_t aph = (uint32_t)((NBUF == 2 ? (it >> 1) : it) & 1);
         ++it;
         if (!wait_bar(&tempty[acc], aph ^ 1, p.err, 12)) break;
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * MB * BN);
         if (tl.kiters == 0) {
           ptx::mbar_arrive(&tfull[acc]);
           continue;
@@ -506,11 +515,15 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t b_base = a_base + A_BYTES;
 #pragma unroll
           for (int ks = 0; ks < BKE / KT::kMmaK; ++ks) {
-            const uint64_t ad = A_MN ? smem_desc(a_base + ks * kMnStep, BOX_BYTES, kMnSbo, kMnLayout)
-                                     : smem_desc(a_base + ks * 32, 16, 1024);
             const uint64_t bd = B_MN ? smem_desc(b_base + ks * kMnStep, BOX_BYTES, kMnSbo, kMnLayout)
                                      : smem_desc(b_base + ks * 32, 16, 1024);
-            mma_issue<KIND>(d_tmem, ad, bd, idesc, (kb | ks) != 0);
+#pragma unroll
+            for (int h = 0; h < MB; ++h) {  // 128-row block h of A into accumulator h
+              const uint32_t ah = a_base + (uint32_t)h * (BM * 128);
+              const uint64_t ad = A_MN ? smem_desc(ah + ks * kMnStep, BOX_BYTES, kMnSbo, kMnLayout)
+                                       : smem_desc(ah + ks * 32, 16, 1024);
+              mma_issue<KIND>(d_tmem + (uint32_t)(h * BN), ad, bd, idesc, (kb | ks) != 0);
+            }
           }
           mma_commit(&empty[s]);
           if (++s == STAGES) { s = 0; ph ^= 1; }
@@ -526,31 +539,34 @@ __global__ void __launch_bounds__(kThreads, 1)
     const bool tma_out = kRing && p.tma_store;
     int it = 0;
     for (int t = blockIdx.x; t < tiles_loop; t += gridDim.x) {
-      const Tile tl = decode<BN, MODE, EPI, BKE>(p, t, order, ntiles);
+      const Tile tl = decode<BN, MODE, EPI, BKE, MB>(p, t, order, ntiles);
       if (!tl.valid) continue;
-      const int acc = it & 1;
-      const uint32_t aph = (uint32_t)((it >> 1) & 1);
+      const int acc = NBUF == 2 ? (it & 1) : 0;
+      const uint32_t aph = (uint32_t)((NBUF == 2 ? (it >> 1) : it) & 1);
       ++it;
       if (!wait_bar(&tfull[acc], aph, p.err, 14)) break;
       tc_fence_after();
-      const uint32_t tbase = tmem_base + (uint32_t)(acc * BN) + ((uint32_t)(q * 32) << 16);
+      const uint32_t tbase = tmem_base + (uint32_t)(acc * MB * BN) + ((uint32_t)(q * 32) << 16);
       const bool zero = tl.kiters == 0;
       const int row0 = tl.m0 + q * 32;  // first row of this warp's 32-row slab
       if (MODE == MODE_K) {
         // tcgen05.ld is warp-collective: every lane loads, only rows < M store.
-        const int m = tl.m0 + row_in_tile;
-        T* dst = static_cast<T*>(p.out0) + ((int64_t)tl.e * p.M + m) * p.ld0 + tl.n0;
 #pragma unroll 1
-        for (int c = 0; c < BN; c += 32) {
-          float v[32];
-          if (zero) {
+        for (int h = 0; h < MB; ++h) {  // accumulator h holds rows m0 + 128h ..
+          const int m = tl.m0 + h * BM + row_in_tile;
+          T* dst = static_cast<T*>(p.out0) + ((int64_t)tl.e * p.M + m) * p.ld0 + tl.n0;
+#pragma unroll 1
+          for (int c = 0; c < BN; c += 32) {
+            float v[32];
+            if (zero) {
 #pragma unroll
-            for (int i = 0; i < 32; ++i) v[i] = 0.f;
-          } else {
-            tmem_ld32(tbase + c, v);
+              for (int i = 0; i < 32; ++i) v[i] = 0.f;
+            } else {
+              tmem_ld32(tbase + (uint32_t)(h * BN) + c, v);
+            }
+            if (tma_out) ring.put(&tmC0, tl.n0 + c, tl.e * p.M + row0 + h * BM, v, lane);
+            else if (m < p.M) store32(dst + c, v);
           }
-          if (tma_out) ring.put(&tmC0, tl.n0 + c, tl.e * p.M + row0, v, lane);
-          else if (m < p.M) store32(dst + c, v);
         }
       } else {
         const int64_t row = tl.m0 + row_in_tile;
@@ -709,15 +725,16 @@ constexpr CUtensorMapSwizzle mn_swizzle() {
   return KIND == KIND_TF32X3 ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B;
 }
 
-template <int BN, bool A_MN, bool B_MN, int MODE, int EPI, int KIND, bool ROWW = false>
+template <int BN, bool A_MN, bool B_MN, int MODE, int EPI, int KIND, bool ROWW = false, int MB = 1>
 int launch(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& c0,
            const CUtensorMap& c1, const CUtensorMap& a2, const CUtensorMap& b2, const Params& p,
            int max_tiles, cudaStream_t st, int max_ctas) {
   constexpr bool kRing = sizeof(typename KindT<KIND>::T) == 2;
-  constexpr int STAGE_BYTES = (BM + BN) * 128;
-  constexpr int STAGES = (BN == 256) ? 4 : (BN == 128 ? 6 : 8);
+  constexpr int STAGE_BYTES = (MB * BM + BN) * 128;
+  constexpr int STAGES = MB == 2 ? 3 : ((BN == 256) ? 4 : (BN == 128 ? 6 : 8));
   constexpr int SMEM = STAGES * STAGE_BYTES + (kRing ? 4 * (int)kRingBytesPerWarp : 0) + 1024 + 256;
-  auto k = moe_gemm_kernel<BN, STAGES, A_MN, B_MN, MODE, EPI, KIND, ROWW>;
+  static_assert(SMEM <= 232448, "shared memory per CTA");
+  auto k = moe_gemm_kernel<BN, STAGES, A_MN, B_MN, MODE, EPI, KIND, ROWW, MB>;
   cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
   int grid = num_sms();
   if (max_ctas > 0 && max_ctas < grid) grid = max_ctas;  // SMs left to concurrent work
@@ -1023,11 +1040,20 @@ int gemm_wgrad(const void* a, const void* a2, int m_dim, const void* b, const vo
   p.out0 = dw;
   p.ld0 = n_dim;
   p.err = err_flag;
-  const int max_tiles = n_experts * ((m_dim + BM - 1) / BM) * (n_dim / bn);
+  int max_tiles = n_experts * ((m_dim + BM - 1) / BM) * (n_dim / bn);
   // TMA stores need every 128-row tile inside one expert's [m_dim, n_dim] block.
   CUtensorMap mc0 = ma;
   p.tma_store = (ES == 2 && m_dim % BM == 0) ? 1 : 0;
   if (p.tma_store && (st = make_out_map<KIND>(&mc0, dw, (int64_t)n_experts * m_dim, n_dim, n_dim))) return st;
+  // An expert whose 128 x 256 tiles outnumber the SMs would run them in several waves, each
+  // streaming the expert's token segment again; 256-row tiles keep it to one wave.
+  if constexpr (ES == 2) {
+    if (bn == 256 && m_dim % (2 * BM) == 0 && p.tma_store && (m_dim / BM) * (n_dim / bn) > num_sms()) {
+      max_tiles = n_experts * (m_dim / (2 * BM)) * (n_dim / bn);
+      return launch<256, true, true, MODE_K, EPI_STORE, KIND, false, 2>(ma, mb, mc0, mc0, ma2, mb2,
+                                                                       p, max_tiles, s, max_ctas);
+    }
+  }
   if constexpr (KIND == KIND_BF16) {
     FK_BN_SWITCH(bn, return (launch<BN_, true, true, MODE_K, EPI_STORE, KIND>(ma, mb, mc0, mc0, ma2, mb2, p, max_tiles, s, max_ctas)));
   } else {

@@ -254,6 +254,35 @@ def test_row_weighted_epilogues(n, k, E, D, H):
                   te, nm, None, sw.data_ptr(), h1w.data_ptr(), actw.data_ptr(), 0, eptr, st)
 
 
+@pytest.mark.parametrize("n,k,E,skew", [(700, 2, 4, 2.0), (96, 4, 8, 0.0)])
+def test_wgrad_256_row_tiles(n, k, E, skew):
+    """Weight gradients whose experts have more 128 x 256 tiles than the GPU has SMs
+    (dW13 at dim 4096, hidden 1024: 256 tiles) run 256-row tiles (two TMEM accumulators per
+    CTA); they match PyTorch fp32 per expert, including experts with no tokens."""
+    D, H = 4096, 1024
+    P = make_problem(n, k, E, D, H, seed=17 + n, skew=skew)
+    plan, R, st = P["plan"], P["plan"].max_rows, P["st"]
+    seg = plan.seg_start
+    eptr = plan.err.data_ptr() + 4
+    G = gen(3)
+    rows = plan.n_mblk.item() * 128
+    valid = (plan.sorted_assign[:rows] >= 0)[:, None]
+    dh1 = torch.zeros(R, 2 * H, dtype=torch.bfloat16, device=DEV)
+    dh1[:rows] = torch.where(valid, torch.randn(rows, 2 * H, generator=G).bfloat16().to(DEV), 0)
+    dw13 = torch.empty(E, 2 * H, D, dtype=torch.bfloat16, device=DEV)
+    _lib.call("fk_moe_gemm_wgrad", dh1.data_ptr(), 2 * H, P["xs"].data_ptr(), D, R,
+              seg.data_ptr(), E, dw13.data_ptr(), 0, eptr, st)
+    torch.cuda.synchronize()
+    assert plan.err[1].item() == 0
+    segs = seg.cpu().tolist()
+    for e in range(E):
+        a, b = segs[e], segs[e + 1]
+        if b == a:
+            assert torch.count_nonzero(dw13[e]) == 0
+        else:
+            close(dw13[e], dh1[a:b].float().t() @ P["xs"][a:b].float())
+
+
 @pytest.mark.parametrize("cap", [1, 7, 100])
 def test_gemm_grid_cap_is_bitwise_neutral(cap):
     """max_ctas only changes which CTA computes a tile, never the tile's arithmetic: every
