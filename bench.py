@@ -717,23 +717,38 @@ class MoELayer(Workload):
 
     def e2e_setup(self):
         self.sink = PinnedSink()
+        self.copy_stream = torch.cuda.Stream(self.dev)
 
     def e2e_step(self):
         """x, dout in; out, dx, the router gradient and the gradient of every expert weight
-        this GPU holds back to pinned host memory."""
+        this GPU holds back to pinned host memory.  The upload of dout overlaps the forward
+        and the download of out overlaps the backward (a side stream for the copies)."""
         self.sink.start()
         self.layer.zero_grad(set_to_none=True)
+        main, cs = torch.cuda.current_stream(self.dev), self.copy_stream
+        cs.wait_stream(main)  # the previous step's work on these buffers is done
         x = self.x_h.to(self.dev, non_blocking=True).requires_grad_(True)
-        d = self.d_h.to(self.dev, non_blocking=True)
+        with torch.cuda.stream(cs):
+            d = self.d_h.to(self.dev, non_blocking=True)
+            d_ready = torch.cuda.Event()
+            d_ready.record(cs)
         out = self.layer(x)
+        fwd_done = torch.cuda.Event()
+        fwd_done.record(main)
+        with torch.cuda.stream(cs):
+            cs.wait_event(fwd_done)
+            self.sink.put("out", out)
+        out.record_stream(cs)
+        main.wait_event(d_ready)
+        d.record_stream(main)
         out.backward(d)
         if self.world > 1:
             self.layer.allreduce_router_grad()
-        self.sink.put("out", out)
         self.sink.put("dx", x.grad)
         for name, prm in self.layer.named_parameters():
             if prm.grad is not None:
                 self.sink.put(name, prm.grad)
+        main.wait_stream(cs)  # the step ends when every copy has landed
 
     def e2e_bytes(self):
         return self.x_h.numel() * 2 * 2, self.sink.nbytes
