@@ -572,7 +572,7 @@ class MoELayer(Workload):
     metric = "MoE layer fwd+bwd throughput"
     ep_transport = "peer"
     ep_replicate = "auto"
-    ep_overlap_sms = 16
+    ep_overlap_sms = 32
     unit = "tokens/s"
     strong = True  # the 32768 global tokens are split across ranks
     tokens, dim, hidden, E, k = 32768, 4096, 1024, 128, 8
@@ -877,16 +877,16 @@ def run_ours(args):
     torch.cuda.synchronize(dev)
     barrier()
     with ClockSampler(dev.index) as clk:
-        t0 = time.perf_counter()
         ms = time_device(run_step, reps, stream)
-        # keep the GPU loaded for ~1 s so the clock record has samples under load
-        extra = 0
-        while time.perf_counter() - t0 < 1.0 and extra < 20000:
+        ms = max_over_ranks(ms, dev)
+        # keep the GPU loaded for ~1 s so the clock record has samples under load; the
+        # count comes from the max over ranks, so every rank runs the same steps (a step
+        # may hold collectives, which every rank must enter equally often)
+        extra = min(20000, max(0, int(1000.0 / max(ms / reps, 1e-3)) - reps))
+        for _ in range(extra):
             run_step()
-            extra += 1
         torch.cuda.synchronize(dev)
     barrier()
-    ms = max_over_ranks(ms, dev)
     n_steps = reps * inner
     ms_per_step = ms / n_steps
     scale_units = 1 if getattr(wl, "strong", False) else world
@@ -1151,7 +1151,7 @@ def main():
     ap.add_argument("--ep-replicate", choices=["auto", "none"], default="auto",
                     help="auto: replicate the experts hot enough that nearly every token picks "
                          "them on every GPU; none: exactly E/N experts per GPU")
-    ap.add_argument("--ep-overlap-sms", type=int, default=16,
+    ap.add_argument("--ep-overlap-sms", type=int, default=32,
                     help="SMs the expert-parallel backward GEMMs leave free for the replicated "
                          "experts' gradient all-reduce running beside them (N > 1)")
     ap.add_argument("--no-cpu-baseline", action="store_true")

@@ -432,7 +432,7 @@ class ExpertParallelMoEMLP(nn.Module):
 
     def __init__(self, dim: int, hidden_dim: int, n_experts: int, k: int = 2, group=None,
                  placement=None, router_version: str = "v2", transport: str = "peer",
-                 replicated=(), overlap_sms: int = 16):
+                 replicated=(), overlap_sms: int = 32):
         super().__init__()
         assert overlap_sms >= 0
         self.overlap_sms = int(overlap_sms)
