@@ -105,13 +105,6 @@ __device__ __forceinline__ float ex2f(float x) {
 }
 constexpr float kLog2e = 1.4426950408889634f;
 
-// 2^x for a pair of bf16 values (packed in and out).
-__device__ __forceinline__ uint32_t ex2_bf16x2(uint32_t x) {
-  uint32_t y;
-  asm("ex2.approx.ftz.bf16x2 %0, %1;" : "=r"(y) : "r"(x));
-  return y;
-}
-
 template <typename T>
 __device__ __forceinline__ float exp_shift(float x, float m) {  // exp(x - m)
   return ex2f(fmaf(x, kLog2e, -m * kLog2e));
@@ -387,25 +380,6 @@ __global__ void __launch_bounds__(kRowThreads, 1) ce_row_kernel(
         const float2 NS = make_float2(-sub, -sub);
         stream_row<T>(src, nvec, drop, ring, [&](int vv, const Vec16<T>& p) {
           const P2* pp = reinterpret_cast<const P2*>(p.e);
-          if constexpr (std::is_same<T, __nv_bfloat16>::value && !SX) {
-            // bf16 gradient without smoothing: one packed exponential per pair gives the
-            // two bf16 results directly (the exponent argument rounded to bf16 first:
-            // relative error |a| * 2^-9 * ln 2 for an argument a <= 0, below the bf16
-            // output's own rounding for |a| <= 1 and far below 1e-3 absolute beyond).
-            // The packet holding the target keeps the fp32 path below.
-            if (vv != tv) {
-              Vec16<T> o2;
-              uint32_t* op = reinterpret_cast<uint32_t*>(o2.e);
-#pragma unroll
-              for (int i = 0; i < NP; ++i) {
-                const float2 a = __ffma2_rn(P::to_f2(pp[i]), L, C);
-                const __nv_bfloat162 ab = __float22bfloat162_rn(a);
-                op[i] = ex2_bf16x2(*reinterpret_cast<const uint32_t*>(&ab));
-              }
-              st_hint(dst + (int64_t)vv * VN, o2.u, drop);
-              return;
-            }
-          }
           float2 g[NP];
 #pragma unroll
           for (int i = 0; i < NP; ++i) {
