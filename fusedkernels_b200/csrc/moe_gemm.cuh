@@ -627,12 +627,34 @@ __global__ void __launch_bounds__(kThreads, 1)
           const T* hu = static_cast<const T*>(p.in0) + row * p.ldi0 + p.H + tl.n0;
           T* dg = static_cast<T*>(p.out0) + row * p.ld0 + tl.n0;
           T* du = static_cast<T*>(p.out0) + row * p.ld0 + p.H + tl.n0;
+          // h1's 32 gate and 32 up values of the next chunk are loaded (as raw 16-byte
+          // packets) while the current chunk is computed and stored.
+          constexpr int QP = 32 * (int)sizeof(T) / 16;  // packets per 32 values
+          uint4 ng[QP], nu[QP];
+#pragma unroll
+          for (int j = 0; j < QP; ++j) {
+            ng[j] = reinterpret_cast<const uint4*>(hg)[j];
+            nu[j] = reinterpret_cast<const uint4*>(hu)[j];
+          }
 #pragma unroll 1
           for (int c = 0; c < BN; c += 32) {
             float d[32], g[32], u[32], og[32], ou[32];
+            uint4 cg[QP], cu[QP];
+#pragma unroll
+            for (int j = 0; j < QP; ++j) {
+              cg[j] = ng[j];
+              cu[j] = nu[j];
+            }
+            if (c + 32 < BN) {
+#pragma unroll
+              for (int j = 0; j < QP; ++j) {
+                ng[j] = reinterpret_cast<const uint4*>(hg + c + 32)[j];
+                nu[j] = reinterpret_cast<const uint4*>(hu + c + 32)[j];
+              }
+            }
             tmem_ld32(tbase + c, d);
-            load32(hg + c, g);
-            load32(hu + c, u);
+            load32(reinterpret_cast<const T*>(cg), g);
+            load32(reinterpret_cast<const T*>(cu), u);
 #pragma unroll
             for (int i = 0; i < 32; ++i) {
               const float sg = sigmoidf_t<T>(g[i]);
