@@ -37,6 +37,7 @@ namespace {
 
 constexpr int kPutThreads = 256;
 constexpr int kPutBatch = 8;  // 16-byte packets per lane in flight in the row copy
+constexpr int kCombineBatch = 4;  // packets per lane accumulated at a time in the combine
 
 // ctl layout (uint32, local to each rank): [phase]       ticket of the put kernels
 //                                          [8 + phase]   sequence numbers published
@@ -154,6 +155,48 @@ __global__ void __launch_bounds__(kPutThreads) ep_peer_combine_put_kernel(
     const int s = (int)(j / T);
     const int64_t dst_row = (int64_t)me * T + (j - (int64_t)s * T);
     T_* dst = static_cast<T_*>(row_bases[s]) + dst_row * dim;
+    if (k <= 32) {
+      // Lane i holds slot i's row and weight; the local slots are walked in slot order
+      // (the same summation order as below), kCombineBatch packets per lane at a time, so
+      // every lane keeps that many loads in flight ahead of its NVLink stores.
+      const int my_p = lane < k ? slot_pos[j * k + lane] : -1;
+      const float my_w = (lane < k && w) ? w[j * k + lane] : 1.0f;
+      const unsigned live = __ballot_sync(0xffffffffu, my_p >= 0);
+      for (int v0 = 0; v0 < nvec; v0 += 32 * kCombineBatch) {
+        float acc[kCombineBatch][V::N];
+#pragma unroll
+        for (int b = 0; b < kCombineBatch; ++b)
+#pragma unroll
+          for (int q = 0; q < V::N; ++q) acc[b][q] = 0.f;
+        for (unsigned m = live; m != 0u; m &= m - 1u) {
+          const int i = __ffs(m) - 1;
+          const int p = __shfl_sync(0xffffffffu, my_p, i);
+          const float wi = __shfl_sync(0xffffffffu, my_w, i);
+          V r[kCombineBatch];
+#pragma unroll
+          for (int b = 0; b < kCombineBatch; ++b) {
+            const int v = v0 + b * 32 + lane;
+            if (v < nvec) r[b] = ld_keep(y + (int64_t)p * dim + v * V::N);
+          }
+#pragma unroll
+          for (int b = 0; b < kCombineBatch; ++b)
+#pragma unroll
+            for (int q = 0; q < V::N; ++q) acc[b][q] = fmaf(wi, Elt<T_>::to_f(r[b].e[q]), acc[b][q]);
+        }
+#pragma unroll
+        for (int b = 0; b < kCombineBatch; ++b) {
+          const int v = v0 + b * 32 + lane;
+          if (v >= nvec) continue;
+          V o;
+#pragma unroll
+          for (int q = 0; q < V::N; ++q) o.e[q] = Elt<T_>::from_f(acc[b][q]);
+          st_plain(dst + v * V::N, o);
+        }
+      }
+      if (dw_rows != nullptr && lane < k)
+        static_cast<float*>(dw_bases[s])[dst_row * k + lane] = dw_rows[j * k + lane];
+      continue;
+    }
     for (int v = lane; v < nvec; v += 32) {
       float acc[V::N];
 #pragma unroll
