@@ -148,6 +148,44 @@ __global__ void __launch_bounds__(256) ep_unpack_sum_kernel(const T_* __restrict
   const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
   const int lane = threadIdx.x & 31;
   for (int64_t t = warp; t < T; t += nwarps) {
+    if (n_ranks <= 32) {
+      // Lane d holds rank d's row position; the ranks holding a partial row are summed in
+      // rank order (as below), 4 packets per lane at a time to keep loads in flight.
+      constexpr int B = 4;
+      const int my_p = lane < n_ranks ? src_pos[t * n_ranks + lane] : -1;
+      const unsigned live = __ballot_sync(0xffffffffu, my_p >= 0);
+      for (int v0 = 0; v0 < nvec; v0 += 32 * B) {
+        float acc[B][V::N];
+#pragma unroll
+        for (int b = 0; b < B; ++b)
+#pragma unroll
+          for (int i = 0; i < V::N; ++i) acc[b][i] = 0.f;
+        for (unsigned m = live; m != 0u; m &= m - 1u) {
+          const int d = __ffs(m) - 1;
+          const int p = __shfl_sync(0xffffffffu, my_p, d);
+          V r[B];
+#pragma unroll
+          for (int b = 0; b < B; ++b) {
+            const int v = v0 + b * 32 + lane;
+            if (v < nvec) r[b] = ld_keep(back + ((int64_t)d * T + p) * dim + v * V::N);
+          }
+#pragma unroll
+          for (int b = 0; b < B; ++b)
+#pragma unroll
+            for (int i = 0; i < V::N; ++i) acc[b][i] += Elt<T_>::to_f(r[b].e[i]);
+        }
+#pragma unroll
+        for (int b = 0; b < B; ++b) {
+          const int v = v0 + b * 32 + lane;
+          if (v >= nvec) continue;
+          V o;
+#pragma unroll
+          for (int i = 0; i < V::N; ++i) o.e[i] = Elt<T_>::from_f(acc[b][i]);
+          st_plain(out + t * dim + v * V::N, o);
+        }
+      }
+      continue;
+    }
     for (int v = lane; v < nvec; v += 32) {
       float acc[V::N];
 #pragma unroll
