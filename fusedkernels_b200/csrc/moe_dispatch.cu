@@ -207,6 +207,45 @@ __global__ void __launch_bounds__(256) moe_combine_kernel(const T* __restrict__ 
   const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
   const int lane = threadIdx.x & 31;
   for (int64_t t = warp; t < n_tokens; t += nwarps) {
+    if (k <= 32) {
+      // Lane j holds slot j's row and weight; the slots are summed in slot order (as
+      // below), kRowBatch packets per lane at a time to keep loads in flight.
+      const int my_p = lane < k ? slot_pos[t * k + lane] : -1;
+      const float my_w = (lane < k && w) ? w[t * k + lane] : 1.0f;
+      const unsigned live = __ballot_sync(0xffffffffu, my_p >= 0);
+      for (int v0 = 0; v0 < nvec; v0 += 32 * kRowBatch) {
+        float acc[kRowBatch][V::N];
+#pragma unroll
+        for (int b = 0; b < kRowBatch; ++b)
+#pragma unroll
+          for (int i = 0; i < V::N; ++i) acc[b][i] = 0.f;
+        for (unsigned m = live; m != 0u; m &= m - 1u) {
+          const int j = __ffs(m) - 1;
+          const int p = __shfl_sync(0xffffffffu, my_p, j);
+          const float wj = __shfl_sync(0xffffffffu, my_w, j);
+          V r[kRowBatch];
+#pragma unroll
+          for (int b = 0; b < kRowBatch; ++b) {
+            const int v = v0 + b * 32 + lane;
+            if (v < nvec) r[b] = ld_keep(y + (int64_t)p * dim + v * V::N);
+          }
+#pragma unroll
+          for (int b = 0; b < kRowBatch; ++b)
+#pragma unroll
+            for (int i = 0; i < V::N; ++i) acc[b][i] = fmaf(wj, Elt<T>::to_f(r[b].e[i]), acc[b][i]);
+        }
+#pragma unroll
+        for (int b = 0; b < kRowBatch; ++b) {
+          const int v = v0 + b * 32 + lane;
+          if (v >= nvec) continue;
+          V o;
+#pragma unroll
+          for (int i = 0; i < V::N; ++i) o.e[i] = Elt<T>::from_f(acc[b][i]);
+          st_plain(out + t * dim + v * V::N, o);
+        }
+      }
+      continue;
+    }
     for (int v = lane; v < nvec; v += 32) {
       float acc[V::N];
 #pragma unroll
