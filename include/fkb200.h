@@ -175,15 +175,17 @@ FK_API int fk_moe_route_meta(const int64_t* idx, const float* w, int64_t n_token
 FK_API int fk_moe_gather(const void* x, int dim, const int* sorted_assign, int k,
                          const int* n_mblk, int64_t max_rows, void* xs, int dtype, void* stream);
 
-/* out[t, :] = sum_j w[t,j] * y[slot_pos[t*k+j], :] (w == NULL: plain sum), fp32
+/* out[t, :] = sum_j w[t,j] * y[slot_pos[t*k+j], :] (w == NULL: plain sum, as after
+ * fk_moe_gemm_up_weighted, whose rows already carry the routing weight), fp32
  * accumulation in slot order (deterministic).
  * Replaces the weight multiply and index_add_ of moe_layer_sorted.py:82-85. */
 FK_API int fk_moe_combine(const void* y, int dim, const int* slot_pos, const float* w,
                           int64_t n_tokens, int k, void* out, int dtype, void* stream);
 
-/* Backward of fk_moe_combine: dy[p, :] = sorted_w[p] * dout[token(p), :] (zero on padding
- * rows) and dw[a] = <dout[token(a), :], y[slot_pos[a], :]> for every assignment a.
- * Replaces the autograd of moe_layer_sorted.py:82-85. */
+/* Backward of the weighted fk_moe_combine: dy[p, :] = sorted_w[p] * dout[token(p), :] (zero
+ * on padding rows) and dw[a] = <dout[token(a), :], y[slot_pos[a], :]> for every assignment
+ * a.  Replaces the autograd of moe_layer_sorted.py:82-85 (the fp16 and fp32 layers; bf16
+ * layers use the row-weighted GEMMs below and fk_moe_dw_from_parts instead). */
 FK_API int fk_moe_combine_bwd(const void* dout, const void* y, int dim,
                               const int* sorted_assign, const float* sorted_w, int k,
                               const int* n_mblk, int64_t max_rows, void* dy, float* dw,
