@@ -38,6 +38,7 @@ SIGNATURES: dict[str, list] = {
     "fk_moe_route_meta": [_vp, _vp, _i64, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64,
                           _vp, _sz, _vp, _vp],
     "fk_moe_gather": [_vp, _i32, _vp, _i32, _vp, _i64, _vp, _i32, _vp],
+    "fk_moe_gather_by_token": [_vp, _i32, _vp, _i64, _i32, _vp, _vp, _i64, _vp, _i32, _vp],
     "fk_moe_combine": [_vp, _i32, _vp, _vp, _i64, _i32, _vp, _i32, _vp],
     "fk_moe_combine_bwd": [_vp, _vp, _i32, _vp, _vp, _i32, _vp, _i64, _vp, _vp, _i32, _vp],
     "fk_moe_gemm_up": [_vp, _i64, _i32, _vp, _i32, _i32, _vp, _vp, _vp, _vp, _i32, _vp, _vp],

@@ -193,6 +193,67 @@ __global__ void __launch_bounds__(256) moe_gather_kernel(const T* __restrict__ x
   }
 }
 
+// The same rows as moe_gather_kernel, walked by token: each token row is read once and
+// stored to the sorted rows of its k slots (the row-order walk reads a token row once per
+// slot, and x is larger than L2 at the workload's size); padding rows are zeroed after.
+template <typename T>
+__global__ void __launch_bounds__(256) moe_gather_by_token_kernel(
+    const T* __restrict__ x, int dim, const int* __restrict__ slot_pos, int64_t n_tokens, int k,
+    const int* __restrict__ sorted_assign, const int* __restrict__ n_mblk, T* __restrict__ xs) {
+  using V = Vec16<T>;
+  const int nvec = dim / V::N;
+  const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  for (int64_t t = warp; t < n_tokens; t += nwarps) {
+    const int my_p = lane < k ? slot_pos[t * k + lane] : -1;
+    unsigned live = __ballot_sync(0xffffffffu, my_p >= 0);
+    if (k > 32) {  // slots past the first 32 (rare): any live one makes the row needed
+      bool more = false;
+      for (int j = 32 + lane; j < k; j += 32) more |= slot_pos[t * k + j] >= 0;
+      if (__any_sync(0xffffffffu, more)) live |= 0x80000000u;  // forces the slow slot loop
+    }
+    if (live == 0u) continue;
+    const T* src = x + t * dim;
+    for (int v0 = 0; v0 < nvec; v0 += 32 * kRowBatch) {
+      V buf[kRowBatch];
+#pragma unroll
+      for (int b = 0; b < kRowBatch; ++b) {
+        const int v = v0 + b * 32 + lane;
+        if (v < nvec) buf[b] = ld_stream(src + v * V::N);
+      }
+      if (k <= 32) {
+        for (unsigned m = live; m != 0u; m &= m - 1u) {
+          const int p = __shfl_sync(0xffffffffu, my_p, __ffs(m) - 1);
+#pragma unroll
+          for (int b = 0; b < kRowBatch; ++b) {
+            const int v = v0 + b * 32 + lane;
+            if (v < nvec) st_plain(xs + (int64_t)p * dim + v * V::N, buf[b]);
+          }
+        }
+      } else {
+        for (int j = 0; j < k; ++j) {
+          const int p = slot_pos[t * k + j];
+          if (p < 0) continue;
+#pragma unroll
+          for (int b = 0; b < kRowBatch; ++b) {
+            const int v = v0 + b * 32 + lane;
+            if (v < nvec) st_plain(xs + (int64_t)p * dim + v * V::N, buf[b]);
+          }
+        }
+      }
+    }
+  }
+  const int64_t rows = (int64_t)(*n_mblk) * kBlockRows;
+  V z;
+  z.u = make_uint4(0, 0, 0, 0);
+  for (int64_t p = warp; p < rows; p += nwarps) {
+    if (sorted_assign[p] >= 0) continue;
+    T* dst = xs + p * dim;
+    for (int v = lane; v < nvec; v += 32) st_plain(dst + v * V::N, z);
+  }
+}
+
 // out[t, :] = sum_j (w ? w[t,j] : 1) * y[slot_pos[t*k+j], :], fp32 accumulation in slot
 // order (deterministic).
 template <typename T>
@@ -433,6 +494,26 @@ extern "C" int fk_moe_gather(const void* x, int dim, const int* sorted_assign, i
                                static_cast<const scalar_t*>(x), dim, sorted_assign, k, n_mblk,
                                static_cast<scalar_t*>(xs)));
   return fk::launch_status("fk_moe_gather");
+}
+
+extern "C" int fk_moe_gather_by_token(const void* x, int dim, const int* slot_pos,
+                                      int64_t n_tokens, int k, const int* sorted_assign,
+                                      const int* n_mblk, int64_t max_rows, void* xs, int dtype,
+                                      void* stream) {
+  FK_CHECK_ARG(x && slot_pos && sorted_assign && n_mblk && xs && k >= 1 && max_rows >= 0 &&
+                   n_tokens >= 0,
+               "fk_moe_gather_by_token: bad argument");
+  FK_CHECK_ARG(fk::valid_dtype(dtype) && dim > 0 && (dim * fk::dtype_size(dtype)) % 16 == 0,
+               "fk_moe_gather_by_token: dim*elt must be a multiple of 16 bytes");
+  FK_CHECK_ARG(fk::aligned16(x) && fk::aligned16(xs), "fk_moe_gather_by_token: unaligned buffers");
+  if (max_rows == 0) return FK_OK;
+  cudaStream_t st = fk::as_stream(stream);
+  const int64_t work = n_tokens > max_rows ? n_tokens : max_rows;
+  FK_DISPATCH_DTYPE(dtype, fk::moe_gather_by_token_kernel<scalar_t>
+                    <<<fk::rows_grid(work), 256, 0, st>>>(
+                        static_cast<const scalar_t*>(x), dim, slot_pos, n_tokens, k,
+                        sorted_assign, n_mblk, static_cast<scalar_t*>(xs)));
+  return fk::launch_status("fk_moe_gather_by_token");
 }
 
 extern "C" int fk_moe_combine(const void* y, int dim, const int* slot_pos, const float* w,

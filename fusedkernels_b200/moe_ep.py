@@ -277,8 +277,9 @@ class _EPMoEFn(torch.autograd.Function):
         h1 = torch.empty(R, 2 * H, **bf)
         act = torch.empty(R, H, **bf)
         y = torch.empty(R, d, **bf)
-        _lib.call("fk_moe_gather", recv_x_p, d, plan.sorted_assign.data_ptr(), k,
-                  plan.n_mblk.data_ptr(), R, xs.data_ptr(), _lib.FK_BF16, st)
+        _lib.call("fk_moe_gather_by_token", recv_x_p, d, plan.slot_pos.data_ptr(), R_tok, k,
+                  plan.sorted_assign.data_ptr(), plan.n_mblk.data_ptr(), R, xs.data_ptr(),
+                  _lib.FK_BF16, st)
         # routing weights applied in the up-projection's epilogue (act = w * silu(g) * u):
         # the expert rows come out weighted and the local slots are summed unweighted
         _lib.call("fk_moe_gemm_up_weighted", xs.data_ptr(), R, d, layer.w13.data_ptr(), H, El,
@@ -347,7 +348,8 @@ class _EPMoEFn(torch.autograd.Function):
         # dy: the received output-gradient rows, unweighted; the down-projection's input
         # gradient applies the routing weight and forms the routing-weight gradient
         sa, sw = plan.sorted_assign.data_ptr(), plan.sorted_w.data_ptr()
-        _lib.call("fk_moe_gather", recv_d_p, d, sa, k, nm, R, dy.data_ptr(), _lib.FK_BF16, st)
+        _lib.call("fk_moe_gather_by_token", recv_d_p, d, plan.slot_pos.data_ptr(), R_tok, k, sa,
+                  nm, R, dy.data_ptr(), _lib.FK_BF16, st)
         part = torch.empty(R, H // 64, dtype=torch.float32, device=dev)
 
         def wgrad(lo, hi, cap, which):

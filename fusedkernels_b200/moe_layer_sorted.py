@@ -6,7 +6,8 @@ ModuleList of ``Expert``), same state_dict keys and the same forward semantics
 (out[t] = sum_j w[t,j] * Expert_{idx[t,j]}(x[t])).  The body differs:
 
   router GEMM (nn.Linear) -> fused_moe_route_v2 -> fk_moe_route_meta (stable counting sort,
-  128-row padded expert segments, all on the device) -> fk_moe_gather -> fk_moe_gemm_up_weighted
+  128-row padded expert segments, all on the device) -> fk_moe_gather_by_token ->
+  fk_moe_gemm_up_weighted
   (tcgen05 grouped GEMM, SwiGLU and routing-weight epilogue) -> fk_moe_gemm_down ->
   fk_moe_combine (per-token fp32 sum in slot order: deterministic, no index_add_ atomics).
 
@@ -115,8 +116,8 @@ class _SortedMoEFn(torch.autograd.Function):
             out = torch.empty(n, d, **td)
             if R > 0:
                 te, nm = plan.tile_expert.data_ptr(), plan.n_mblk.data_ptr()
-                _lib.call("fk_moe_gather", x.data_ptr(), d, plan.sorted_assign.data_ptr(), k,
-                          nm, R, xs.data_ptr(), code, st)
+                _lib.call("fk_moe_gather_by_token", x.data_ptr(), d, plan.slot_pos.data_ptr(), n,
+                          k, plan.sorted_assign.data_ptr(), nm, R, xs.data_ptr(), code, st)
                 _lib.call("fk_moe_gemm_up_weighted", xs.data_ptr(), R, d, layer.w13.data_ptr(),
                           H, E, te, nm, plan.sorted_assign.data_ptr(), plan.sorted_w.data_ptr(),
                           h1.data_ptr(), act_w.data_ptr(), 0, eptr + 4, st)
@@ -254,7 +255,8 @@ class _SortedMoEFn(torch.autograd.Function):
             te, nm, seg = plan.tile_expert.data_ptr(), plan.n_mblk.data_ptr(), plan.seg_start.data_ptr()
             sa, sw = plan.sorted_assign.data_ptr(), plan.sorted_w.data_ptr()
             dy = torch.empty(R, d, **td)
-            _lib.call("fk_moe_gather", dout.data_ptr(), d, sa, k, nm, R, dy.data_ptr(), code, st)
+            _lib.call("fk_moe_gather_by_token", dout.data_ptr(), d, plan.slot_pos.data_ptr(), n,
+                      k, sa, nm, R, dy.data_ptr(), code, st)
             dh1 = torch.empty(R, 2 * H, **td)
             part = torch.empty(R, H // 64, dtype=torch.float32, device=dev)
             _lib.call("fk_moe_gemm_down_dgrad_weighted", dy.data_ptr(), R, d, layer.w2.data_ptr(),

@@ -175,6 +175,14 @@ FK_API int fk_moe_route_meta(const int64_t* idx, const float* w, int64_t n_token
 FK_API int fk_moe_gather(const void* x, int dim, const int* sorted_assign, int k,
                          const int* n_mblk, int64_t max_rows, void* xs, int dtype, void* stream);
 
+/* Same result as fk_moe_gather, walked by token: each of the n_tokens rows of x is read once
+ * and stored to the sorted rows of its slots (slot_pos[t*k+j], -1 = slot not gathered), then
+ * the padding rows (sorted_assign < 0) are zeroed.  The row-order walk reads a token row once
+ * per slot; this one reads x once.  Replaces the same line, moe_layer_sorted.py:63. */
+FK_API int fk_moe_gather_by_token(const void* x, int dim, const int* slot_pos, int64_t n_tokens,
+                                  int k, const int* sorted_assign, const int* n_mblk,
+                                  int64_t max_rows, void* xs, int dtype, void* stream);
+
 /* out[t, :] = sum_j w[t,j] * y[slot_pos[t*k+j], :] (w == NULL: plain sum, as after
  * fk_moe_gemm_up_weighted, whose rows already carry the routing weight), fp32
  * accumulation in slot order (deterministic).

@@ -197,6 +197,22 @@ def test_gemm_backward_pieces(n, k, E, D, H):
 
 
 @pytest.mark.parametrize("n,k,E,D,H", SHAPES)
+def test_gather_by_token_equals_row_gather(n, k, E, D, H):
+    """The token-order gather writes the same sorted rows as the row-order gather, bit for
+    bit (padding rows zero), and leaves the rows past the last valid block alone."""
+    P = make_problem(n, k, E, D, H, seed=11 * n + D)
+    plan, R, st = P["plan"], P["plan"].max_rows, P["st"]
+    rows = plan.n_mblk.item() * 128
+    xs = torch.full((R, D), float("nan"), dtype=torch.bfloat16, device=DEV)
+    _lib.call("fk_moe_gather_by_token", P["x"].data_ptr(), D, plan.slot_pos.data_ptr(), n, k,
+              plan.sorted_assign.data_ptr(), plan.n_mblk.data_ptr(), R, xs.data_ptr(),
+              _lib.FK_BF16, st)
+    torch.cuda.synchronize()
+    assert torch.equal(xs[:rows], P["xs"][:rows])
+    assert torch.isnan(xs[rows:].float()).all()
+
+
+@pytest.mark.parametrize("n,k,E,D,H", SHAPES)
 def test_row_weighted_epilogues(n, k, E, D, H):
     """The row-weighted GEMM variants against the plain ones and PyTorch fp32: h1
     bit-identical (same operands), act_w = w * act, zero padding rows; the weighted
